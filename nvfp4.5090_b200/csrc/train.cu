@@ -1,0 +1,369 @@
+// Element-wise and row-reduction kernels of the NVFP4 SwiGLU MLP training
+// step (B200, sm_100a).  The reference trains with a bf16 backward
+// (float4utils.py:653-683) and ships no MLP; these kernels carry the
+// activations, gradients and optimizer state between the NVFP4 GEMMs.
+// All are HBM-bound: 16-byte vector accesses, grid sized to the SM count.
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace nvfp4b200 {
+
+static int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev);
+  return cache[dev] > 0 ? cache[dev] : 148;
+}
+
+static unsigned grid_for(int64_t work_items, int threads, int per_sm = 8) {
+  const int64_t want = ceil_div(std::max<int64_t>(work_items, 1), threads);
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sm_count() * per_sm));
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// |bf16 pair| max as float bits (NaN ignored)
+__device__ __forceinline__ uint32_t absmax_word_bits(uint32_t w) {
+  uint32_t a = w & 0x7FFF7FFFu;
+  a &= ~__vcmpgtu2(a, 0x7F807F80u);
+  return max(a & 0xFFFFu, a >> 16) << 16;
+}
+
+// h = silu(gate) * up, 8 columns per thread; optional global amax of h.
+__global__ void __launch_bounds__(256) swiglu_fwd_kernel(const uint16_t* __restrict__ gu, uint16_t* __restrict__ h,
+                                                         int64_t tokens, int64_t ff, uint32_t* ws, float* g_out) {
+  const int64_t vec_per_row = ff / 8;
+  const int64_t total = tokens * vec_per_row;
+  uint32_t m = 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / vec_per_row, c = (i - t * vec_per_row) * 8;
+    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gu + t * 2 * ff + c));
+    const uint4 uv = __ldg(reinterpret_cast<const uint4*>(gu + t * 2 * ff + ff + c));
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float g0 = bf16lo(gw[j]), g1 = bf16hi(gw[j]);
+      const float h0 = g0 * sigmoidf_(g0) * bf16lo(uw[j]);
+      const float h1 = g1 * sigmoidf_(g1) * bf16hi(uw[j]);
+      o[j] = pack2(h0, h1);
+      m = max(m, absmax_word_bits(o[j]));
+    }
+    *reinterpret_cast<uint4*>(h + t * ff + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if (ws) amax_commit(m, ws, g_out, nullptr);
+}
+
+// dgate = dh * up * silu'(gate), dup = dh * silu(gate);
+// silu'(g) = s * (1 + g * (1 - s)), s = sigmoid(g).
+__global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint16_t* __restrict__ gu,
+                                                         const uint16_t* __restrict__ dh, uint16_t* __restrict__ dgu,
+                                                         int64_t tokens, int64_t ff, uint32_t* ws, float* g_out) {
+  const int64_t vec_per_row = ff / 8;
+  const int64_t total = tokens * vec_per_row;
+  uint32_t m = 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / vec_per_row, c = (i - t * vec_per_row) * 8;
+    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gu + t * 2 * ff + c));
+    const uint4 uv = __ldg(reinterpret_cast<const uint4*>(gu + t * 2 * ff + ff + c));
+    const uint4 dv = __ldg(reinterpret_cast<const uint4*>(dh + t * ff + c));
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w},
+                   dw[4] = {dv.x, dv.y, dv.z, dv.w};
+    uint32_t og[4], ou[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float dg[2], du[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float g = e ? bf16hi(gw[j]) : bf16lo(gw[j]);
+        const float u = e ? bf16hi(uw[j]) : bf16lo(uw[j]);
+        const float d = e ? bf16hi(dw[j]) : bf16lo(dw[j]);
+        const float s = sigmoidf_(g);
+        du[e] = d * (g * s);
+        dg[e] = d * u * (s * (1.0f + g * (1.0f - s)));
+      }
+      og[j] = pack2(dg[0], dg[1]);
+      ou[j] = pack2(du[0], du[1]);
+      m = max(m, max(absmax_word_bits(og[j]), absmax_word_bits(ou[j])));
+    }
+    *reinterpret_cast<uint4*>(dgu + t * 2 * ff + c) = make_uint4(og[0], og[1], og[2], og[3]);
+    *reinterpret_cast<uint4*>(dgu + t * 2 * ff + ff + c) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+  }
+  if (ws) amax_commit(m, ws, g_out, nullptr);
+}
+
+// RMSNorm backward.  One CTA (256 threads) walks a band of rows; thread t
+// owns columns {2048*v + 8*t + i}.  Per row: s = sum(dy*gamma*xn) by a
+// block reduction, dx = inv*(dy*gamma - xn*s/k) + dres; dgamma partial sums
+// stay in registers for the whole band and are added to global once.
+constexpr int RB_THREADS = 256;
+template <int NV>
+__global__ void __launch_bounds__(RB_THREADS) rmsnorm_bwd_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma, const float* __restrict__ inv_rms,
+    const uint16_t* __restrict__ dy, const uint16_t* __restrict__ dres, uint16_t* __restrict__ dx,
+    float* __restrict__ dgamma, int64_t rows, int64_t k, int64_t rows_per_cta) {
+  __shared__ float red[2][RB_THREADS / 32];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  float gam[NV][8], dgam[NV][8];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int64_t col = (int64_t)v * 2048 + 8 * tid;
+    uint4 gv = make_uint4(0, 0, 0, 0);
+    if (col < k) gv = gamma ? __ldg(reinterpret_cast<const uint4*>(gamma + col))
+                            : make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+    const uint32_t w[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      gam[v][2 * j] = bf16lo(w[j]);
+      gam[v][2 * j + 1] = bf16hi(w[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dgam[v][j] = 0.0f;
+  }
+  const int64_t r_begin = (int64_t)blockIdx.x * rows_per_cta;
+  const int64_t r_end = imin64(rows, r_begin + rows_per_cta);
+  int buf = 0;
+  for (int64_t r = r_begin; r < r_end; ++r) {
+    const float inv = __ldg(inv_rms + r);
+    float xn[NV][8], dyg[NV][8];
+    float part = 0.0f;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int64_t col = (int64_t)v * 2048 + 8 * tid;
+      uint4 xv = make_uint4(0, 0, 0, 0), dv = make_uint4(0, 0, 0, 0);
+      if (col < k) {
+        xv = __ldg(reinterpret_cast<const uint4*>(x + r * k + col));
+        dv = __ldg(reinterpret_cast<const uint4*>(dy + r * k + col));
+      }
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xn[v][2 * j] = bf16lo(xw[j]) * inv;
+        xn[v][2 * j + 1] = bf16hi(xw[j]) * inv;
+        const float d0 = bf16lo(dw[j]), d1 = bf16hi(dw[j]);
+        dgam[v][2 * j] += d0 * xn[v][2 * j];
+        dgam[v][2 * j + 1] += d1 * xn[v][2 * j + 1];
+        dyg[v][2 * j] = d0 * gam[v][2 * j];
+        dyg[v][2 * j + 1] = d1 * gam[v][2 * j + 1];
+        part += dyg[v][2 * j] * xn[v][2 * j] + dyg[v][2 * j + 1] * xn[v][2 * j + 1];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (lane == 0) red[buf][wid] = part;
+    __syncthreads();
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < RB_THREADS / 32; ++i) s += red[buf][i];
+    buf ^= 1;
+    const float mean = s / (float)k;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int64_t col = (int64_t)v * 2048 + 8 * tid;
+      if (col >= k) continue;
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = inv * (dyg[v][j] - xn[v][j] * mean);
+      if (dres) {
+        const uint4 rv = __ldg(reinterpret_cast<const uint4*>(dres + r * k + col));
+        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          o[2 * j] += bf16lo(rw[j]);
+          o[2 * j + 1] += bf16hi(rw[j]);
+        }
+      }
+      *reinterpret_cast<uint4*>(dx + r * k + col) =
+          make_uint4(pack2(o[0], o[1]), pack2(o[2], o[3]), pack2(o[4], o[5]), pack2(o[6], o[7]));
+    }
+  }
+  if (dgamma) {
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int64_t col = (int64_t)v * 2048 + 8 * tid;
+      if (col >= k) continue;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) atomicAdd(dgamma + col + j, dgam[v][j]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) add_bf16_kernel(const uint16_t* __restrict__ a, const uint16_t* __restrict__ b,
+                                                       uint16_t* __restrict__ y, int64_t n) {
+  const int64_t nv = n / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 av = __ldg(reinterpret_cast<const uint4*>(a) + i), bv = __ldg(reinterpret_cast<const uint4*>(b) + i);
+    const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = pack2(bf16lo(aw[j]) + bf16lo(bw[j]), bf16hi(aw[j]) + bf16hi(bw[j]));
+    reinterpret_cast<uint4*>(y)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  for (int64_t i = nv * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float s = __uint_as_float((uint32_t)a[i] << 16) + __uint_as_float((uint32_t)b[i] << 16);
+    const __nv_bfloat16 hb = __float2bfloat16_rn(s);
+    y[i] = *reinterpret_cast<const uint16_t*>(&hb);
+  }
+}
+
+struct AdamArgs {
+  float lr, b1, b2, eps, wd, bc1, bc2, gscale;
+};
+
+__device__ __forceinline__ float adam_one(float p, float g, float& m, float& v, const AdamArgs& a) {
+  g *= a.gscale;
+  m = a.b1 * m + (1.0f - a.b1) * g;
+  v = a.b2 * v + (1.0f - a.b2) * g * g;
+  const float mh = m / a.bc1, vh = v / a.bc2;
+  return p - a.lr * (mh / (sqrtf(vh) + a.eps) + a.wd * p);
+}
+
+template <bool GRAD_F32>
+__global__ void __launch_bounds__(256) adamw_kernel(uint16_t* __restrict__ p, const void* __restrict__ grad,
+                                                    float* __restrict__ m, float* __restrict__ v, int64_t n,
+                                                    AdamArgs a) {
+  const int64_t nv = n / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 pv = reinterpret_cast<const uint4*>(p)[i];
+    float g[8];
+    if (GRAD_F32) {
+      const float4 g0 = reinterpret_cast<const float4*>(grad)[2 * i], g1 = reinterpret_cast<const float4*>(grad)[2 * i + 1];
+      g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w; g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+    } else {
+      const uint4 gv = reinterpret_cast<const uint4*>(grad)[i];
+      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { g[2 * j] = bf16lo(gw[j]); g[2 * j + 1] = bf16hi(gw[j]); }
+    }
+    float4 m0 = reinterpret_cast<float4*>(m)[2 * i], m1 = reinterpret_cast<float4*>(m)[2 * i + 1];
+    float4 v0 = reinterpret_cast<float4*>(v)[2 * i], v1 = reinterpret_cast<float4*>(v)[2 * i + 1];
+    float mm[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+    float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    const uint32_t pw[4] = {pv.x, pv.y, pv.z, pv.w};
+    float pf[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { pf[2 * j] = bf16lo(pw[j]); pf[2 * j + 1] = bf16hi(pw[j]); }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) pf[j] = adam_one(pf[j], g[j], mm[j], vv[j], a);
+    reinterpret_cast<uint4*>(p)[i] = make_uint4(pack2(pf[0], pf[1]), pack2(pf[2], pf[3]), pack2(pf[4], pf[5]), pack2(pf[6], pf[7]));
+    reinterpret_cast<float4*>(m)[2 * i] = make_float4(mm[0], mm[1], mm[2], mm[3]);
+    reinterpret_cast<float4*>(m)[2 * i + 1] = make_float4(mm[4], mm[5], mm[6], mm[7]);
+    reinterpret_cast<float4*>(v)[2 * i] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+    reinterpret_cast<float4*>(v)[2 * i + 1] = make_float4(vv[4], vv[5], vv[6], vv[7]);
+  }
+  for (int64_t i = nv * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float g = GRAD_F32 ? static_cast<const float*>(grad)[i]
+                             : __uint_as_float((uint32_t)static_cast<const uint16_t*>(grad)[i] << 16);
+    float mm = m[i], vv = v[i];
+    const float r = adam_one(__uint_as_float((uint32_t)p[i] << 16), g, mm, vv, a);
+    m[i] = mm;
+    v[i] = vv;
+    const __nv_bfloat16 hb = __float2bfloat16_rn(r);
+    p[i] = *reinterpret_cast<const uint16_t*>(&hb);
+  }
+}
+
+}  // namespace nvfp4b200
+
+using namespace nvfp4b200;
+
+extern "C" {
+
+int nvfp4b200_swiglu_fwd(const void* gu, void* h, int64_t tokens, int64_t ff, uint32_t* ws, float* global_scale_out,
+                         void* stream) {
+  if (!gu || !h) return NVFP4B200_ERR_INVALID_ARG;
+  if ((ws == nullptr) != (global_scale_out == nullptr)) return NVFP4B200_ERR_INVALID_ARG;
+  if (tokens < 0 || ff <= 0 || ff % 8) return NVFP4B200_ERR_BAD_SHAPE;
+  if (!aligned(gu, 16) || !aligned(h, 16)) return NVFP4B200_ERR_MISALIGNED;
+  int rc = check_device();
+  if (rc) return rc;
+  if (tokens == 0) return NVFP4B200_OK;
+  swiglu_fwd_kernel<<<grid_for(tokens * ff / 8, 256), 256, 0, (cudaStream_t)stream>>>(
+      static_cast<const uint16_t*>(gu), static_cast<uint16_t*>(h), tokens, ff, ws, global_scale_out);
+  return launch_status();
+}
+
+int nvfp4b200_swiglu_bwd(const void* gu, const void* dh, void* dgu, int64_t tokens, int64_t ff, uint32_t* ws,
+                         float* global_scale_out, void* stream) {
+  if (!gu || !dh || !dgu) return NVFP4B200_ERR_INVALID_ARG;
+  if ((ws == nullptr) != (global_scale_out == nullptr)) return NVFP4B200_ERR_INVALID_ARG;
+  if (tokens < 0 || ff <= 0 || ff % 8) return NVFP4B200_ERR_BAD_SHAPE;
+  if (!aligned(gu, 16) || !aligned(dh, 16) || !aligned(dgu, 16)) return NVFP4B200_ERR_MISALIGNED;
+  int rc = check_device();
+  if (rc) return rc;
+  if (tokens == 0) return NVFP4B200_OK;
+  swiglu_bwd_kernel<<<grid_for(tokens * ff / 8, 256), 256, 0, (cudaStream_t)stream>>>(
+      static_cast<const uint16_t*>(gu), static_cast<const uint16_t*>(dh), static_cast<uint16_t*>(dgu), tokens, ff, ws,
+      global_scale_out);
+  return launch_status();
+}
+
+int nvfp4b200_rmsnorm_bwd(const void* x, const void* gamma, const float* inv_rms, const void* dy, const void* dres,
+                          void* dx, float* dgamma_acc, int64_t rows, int64_t k, void* stream) {
+  if (!x || !inv_rms || !dy || !dx) return NVFP4B200_ERR_INVALID_ARG;
+  if (rows < 0 || k <= 0 || k % 8 || k > 4 * 2048) return NVFP4B200_ERR_BAD_SHAPE;
+  if (!aligned(x, 16) || !aligned(dy, 16) || !aligned(dx, 16) || (gamma && !aligned(gamma, 16)) ||
+      (dres && !aligned(dres, 16)) || !aligned(inv_rms, 4))
+    return NVFP4B200_ERR_MISALIGNED;
+  int rc = check_device();
+  if (rc) return rc;
+  if (rows == 0) return NVFP4B200_OK;
+  const int64_t ctas = std::min<int64_t>(rows, (int64_t)sm_count() * 4);
+  const int64_t rpc = ceil_div(rows, ctas);
+  const unsigned grid = (unsigned)ceil_div(rows, rpc);
+  cudaStream_t st = (cudaStream_t)stream;
+  auto X = static_cast<const uint16_t*>(x);
+  auto G = static_cast<const uint16_t*>(gamma);
+  auto DY = static_cast<const uint16_t*>(dy);
+  auto DR = static_cast<const uint16_t*>(dres);
+  auto DX = static_cast<uint16_t*>(dx);
+  const int nv = (int)ceil_div(k, 2048);
+  if (nv <= 1)
+    rmsnorm_bwd_kernel<1><<<grid, RB_THREADS, 0, st>>>(X, G, inv_rms, DY, DR, DX, dgamma_acc, rows, k, rpc);
+  else if (nv <= 2)
+    rmsnorm_bwd_kernel<2><<<grid, RB_THREADS, 0, st>>>(X, G, inv_rms, DY, DR, DX, dgamma_acc, rows, k, rpc);
+  else
+    rmsnorm_bwd_kernel<4><<<grid, RB_THREADS, 0, st>>>(X, G, inv_rms, DY, DR, DX, dgamma_acc, rows, k, rpc);
+  return launch_status();
+}
+
+int nvfp4b200_add_bf16(const void* a, const void* b, void* y, int64_t n, void* stream) {
+  if (!a || !b || !y) return NVFP4B200_ERR_INVALID_ARG;
+  if (n < 0) return NVFP4B200_ERR_BAD_SHAPE;
+  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(y, 16)) return NVFP4B200_ERR_MISALIGNED;
+  int rc = check_device();
+  if (rc) return rc;
+  if (n == 0) return NVFP4B200_OK;
+  add_bf16_kernel<<<grid_for(n / 8 + 1, 256), 256, 0, (cudaStream_t)stream>>>(
+      static_cast<const uint16_t*>(a), static_cast<const uint16_t*>(b), static_cast<uint16_t*>(y), n);
+  return launch_status();
+}
+
+int nvfp4b200_adamw_step(void* param, const void* grad, int grad_dtype, float* m, float* v, int64_t n, float lr,
+                         float beta1, float beta2, float eps, float weight_decay, float bias_corr1, float bias_corr2,
+                         float grad_scale, void* stream) {
+  if (!param || !grad || !m || !v) return NVFP4B200_ERR_INVALID_ARG;
+  if (grad_dtype != NVFP4B200_BF16 && grad_dtype != NVFP4B200_F32) return NVFP4B200_ERR_INVALID_ARG;
+  if (n < 0) return NVFP4B200_ERR_BAD_SHAPE;
+  if (!aligned(param, 16) || !aligned(grad, 16) || !aligned(m, 16) || !aligned(v, 16)) return NVFP4B200_ERR_MISALIGNED;
+  int rc = check_device();
+  if (rc) return rc;
+  if (n == 0) return NVFP4B200_OK;
+  AdamArgs a{lr, beta1, beta2, eps, weight_decay, bias_corr1, bias_corr2, grad_scale};
+  const unsigned grid = grid_for(n / 8 + 1, 256);
+  if (grad_dtype == NVFP4B200_F32)
+    adamw_kernel<true><<<grid, 256, 0, (cudaStream_t)stream>>>(static_cast<uint16_t*>(param), grad, m, v, n, a);
+  else
+    adamw_kernel<false><<<grid, 256, 0, (cudaStream_t)stream>>>(static_cast<uint16_t*>(param), grad, m, v, n, a);
+  return launch_status();
+}
+
+}  // extern "C"

@@ -1,0 +1,75 @@
+"""CPU tests of the C ABI: the library loads, exports every symbol the header
+declares, and rejects invalid arguments before touching any device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "nvfp4_b200.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(nvfp4b200_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_api():
+    names = _declared()
+    for must in ("nvfp4b200_quant_nvfp4", "nvfp4b200_rmsnorm_quant_nvfp4", "nvfp4b200_nvfp4_mm",
+                 "nvfp4b200_nvfp4_mm_relu", "nvfp4b200_nvfp4_mm_relu_2", "nvfp4b200_gemm",
+                 "nvfp4b200_quant_nvfp4_t", "nvfp4b200_global_scale"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg._lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), f"{name} declared in include/nvfp4_b200.h but not exported"
+    # and the Python binding covers the same set
+    assert set(_declared()) == set(pkg._lib.exported_symbols())
+
+
+def test_api_version_matches_header(pkg):
+    lib = pkg._lib.load()
+    m = re.search(r"#define NVFP4B200_API_VERSION (\d+)", open(HEADER).read())
+    assert lib.nvfp4b200_api_version() == int(m.group(1))
+
+
+def test_status_strings(pkg):
+    assert pkg._lib.status_string(0) == "ok"
+    assert "shape" in pkg._lib.status_string(2)
+    assert "aligned" in pkg._lib.status_string(3)
+    assert pkg._lib.status_string(99) == "unknown status"
+
+
+FAKE = 1 << 20            # 16-byte aligned, never dereferenced: validation fails first
+MIS = FAKE + 4
+
+
+@pytest.mark.parametrize("call,expected", [
+    (lambda L: L.nvfp4b200_quant_nvfp4(None, FAKE, FAKE, 4, 32, None, None), 1),
+    (lambda L: L.nvfp4b200_quant_nvfp4(FAKE, FAKE, FAKE, 4, 24, None, None), 2),      # k % 16
+    (lambda L: L.nvfp4b200_quant_nvfp4(FAKE, FAKE, FAKE, -1, 32, None, None), 2),
+    (lambda L: L.nvfp4b200_quant_nvfp4(MIS, FAKE, FAKE, 4, 32, None, None), 3),
+    (lambda L: L.nvfp4b200_quant_nvfp4_t(FAKE, None, None, FAKE, FAKE, 24, 16, None, None), 2),  # rows % 16
+    (lambda L: L.nvfp4b200_rmsnorm_quant_nvfp4(FAKE, None, FAKE, FAKE, None, 4, 32, 1e-6, None, None), 1),
+    (lambda L: L.nvfp4b200_nvfp4_mm(FAKE, FAKE, FAKE, FAKE, None, None, FAKE, 8, 8, 48, None), 2),  # k % 32
+    (lambda L: L.nvfp4b200_nvfp4_mm(FAKE, FAKE, FAKE, FAKE, None, None, FAKE, 8, 12, 64, None), 2),  # n % 8
+    (lambda L: L.nvfp4b200_nvfp4_mm(FAKE, MIS, FAKE, FAKE, None, None, FAKE, 8, 8, 64, None), 3),
+    (lambda L: L.nvfp4b200_nvfp4_mm(None, FAKE, FAKE, FAKE, None, None, FAKE, 8, 8, 64, None), 1),
+    (lambda L: L.nvfp4b200_gemm(FAKE, FAKE, FAKE, FAKE, None, None, None, None, FAKE, 0, 1, 0, 8, 8, 64, 8, None), 1),
+    (lambda L: L.nvfp4b200_gemm(FAKE, FAKE, FAKE, FAKE, None, None, None, None, FAKE, 0, 0, 7, 8, 8, 64, 8, None), 1),
+    (lambda L: L.nvfp4b200_swiglu_fwd(FAKE, FAKE, 4, 12, None, None, None), 2),
+    (lambda L: L.nvfp4b200_adamw_step(FAKE, FAKE, 5, FAKE, FAKE, 8, 1e-3, .9, .95, 1e-8, 0., 1., 1., 1., None), 1),
+])
+def test_argument_validation_without_device(pkg, call, expected):
+    assert call(pkg._lib.load()) == expected
+
+
+def test_python_binding_fails_loudly_without_library(pkg, monkeypatch, tmp_path):
+    monkeypatch.setattr(pkg._lib, "_lib", None)
+    monkeypatch.setattr(pkg._lib, "lib_path", lambda: str(tmp_path / "missing.so"))
+    with pytest.raises(pkg.NVFP4Error):
+        pkg._lib.load()
