@@ -1,0 +1,291 @@
+"""NVFP4 SwiGLU MLP: forward, dgrad and wgrad with NVFP4 operands.
+
+The reference ships only an NVFP4-forward / bf16-backward linear layer
+(float4utils.py:621-714) and mentions an unshipped "NVFP4 MLP" (README.md:1).
+This module builds that MLP block on the library's kernels:
+
+    y  = x + W_down . h,    h = silu(g) * u,    [g | u] = W_gu . n(x),
+    n(x) = (x * inv_rms(x)) * gamma
+
+with W_gu = [W_gate; W_up] ([2F, D]) and W_down ([D, F]).  Every GEMM takes
+NVFP4 operands blocked 1x16 along its contraction dimension with a
+per-tensor global scale g = amax/(6*448) folded into the GEMM's output scale:
+
+    forward   gu  = Q(n(x))     . Q(W_gu)^T          K = D
+              y   = Q(h)        . Q(W_down)^T + x    K = F  (residual fused)
+    dgrad     dh  = Q(dy)       . Q_t(W_down)^T      K = D
+              dxn = Q(dgu)      . Q_t(W_gu)^T        K = 2F
+    wgrad     dWd = Q_t(dy)     . Q_t(h)^T           K = tokens
+              dWgu= Q_t(dgu)    . Q_t(n(x))^T        K = tokens
+
+Q quantizes along rows' last dimension, Q_t along the first (transposed
+quantizer).  Quantization is treated as identity in the backward
+(straight-through).  Weights are quantized once per optimizer step and
+reused across micro-batches.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import torch
+import torch.nn as nn
+
+from . import ops
+
+
+@dataclass
+class QWeights:
+    """Per-step NVFP4 copies of one block's weights (forward and dgrad layouts)."""
+    g_gu: torch.Tensor
+    g_down: torch.Tensor
+    q_gu: torch.Tensor
+    s_gu: torch.Tensor
+    q_down: torch.Tensor
+    s_down: torch.Tensor
+    q_gu_t: torch.Tensor
+    s_gu_t: torch.Tensor
+    q_down_t: torch.Tensor
+    s_down_t: torch.Tensor
+
+
+def quantize_weights(w_gu: torch.Tensor, w_down: torch.Tensor, need_t: bool = True) -> QWeights:
+    g_gu = ops.global_scale(w_gu)
+    g_down = ops.global_scale(w_down)
+    q_gu, s_gu = ops.quantize(w_gu, global_scale=g_gu)
+    q_down, s_down = ops.quantize(w_down, global_scale=g_down)
+    if need_t:
+        q_gu_t, s_gu_t = ops.quantize_t(w_gu, global_scale=g_gu)        # [D, 2F] along 2F
+        q_down_t, s_down_t = ops.quantize_t(w_down, global_scale=g_down)  # [F, D] along D
+    else:
+        q_gu_t = s_gu_t = q_down_t = s_down_t = None
+    return QWeights(g_gu, g_down, q_gu, s_gu, q_down, s_down, q_gu_t, s_gu_t, q_down_t, s_down_t)
+
+
+@dataclass
+class Saved:
+    x: torch.Tensor
+    inv_rms: torch.Tensor
+    g_xn: torch.Tensor
+    gu: torch.Tensor
+    h: torch.Tensor
+    g_h: torch.Tensor
+
+
+def block_forward(x: torch.Tensor, gamma: torch.Tensor, qw: QWeights, eps: float = 1e-6, save: bool = True):
+    """One RMSNorm+SwiGLU block on bf16 x [T, D] -> (y [T, D], saved activations)."""
+    inv_rms, g_xn = ops.rmsnorm_stats(x, eps, gamma=gamma)
+    q_xn, s_xn = ops.quantize(x, global_scale=g_xn, row_scale=inv_rms, gamma=gamma)
+    gu = ops.gemm(q_xn, s_xn, qw.q_gu, qw.s_gu, scale_a=g_xn, scale_b=qw.g_gu)
+    del q_xn, s_xn
+    h, g_h = ops.swiglu_fwd(gu, with_scale=True)
+    q_h, s_h = ops.quantize(h, global_scale=g_h)
+    y = ops.gemm(q_h, s_h, qw.q_down, qw.s_down, scale_a=g_h, scale_b=qw.g_down, residual=x)
+    saved = Saved(x, inv_rms, g_xn, gu, h, g_h) if save else None
+    return y, saved
+
+
+def block_backward(dy: torch.Tensor, gamma: torch.Tensor, qw: QWeights, sv: Saved,
+                   grad_gamma: torch.Tensor, grad_gu: torch.Tensor, grad_down: torch.Tensor,
+                   accumulate: bool) -> torch.Tensor:
+    """Backward of block_forward given dy [T, D].
+
+    grad_gamma (fp32 [D]) is accumulated; grad_gu ([2F, D]) and grad_down
+    ([D, F]) are written (bf16) or accumulated (fp32, accumulate=True).
+    Returns dx [T, D] (including the residual path)."""
+    g_dy = ops.global_scale(dy)
+    q_dy, s_dy = ops.quantize(dy, global_scale=g_dy)
+    dh = ops.gemm(q_dy, s_dy, qw.q_down_t, qw.s_down_t, scale_a=g_dy, scale_b=qw.g_down)
+    del q_dy, s_dy
+    # wgrad of W_down: dy^T . h  (contraction over tokens)
+    q_dyt, s_dyt = ops.quantize_t(dy, global_scale=g_dy)
+    q_ht, s_ht = ops.quantize_t(sv.h, global_scale=sv.g_h)
+    ops.gemm(q_dyt, s_dyt, q_ht, s_ht, scale_a=g_dy, scale_b=sv.g_h, out=grad_down, accumulate=accumulate)
+    del q_dyt, s_dyt, q_ht, s_ht
+    dgu, g_dgu = ops.swiglu_bwd(sv.gu, dh, with_scale=True)
+    del dh
+    q_dgu, s_dgu = ops.quantize(dgu, global_scale=g_dgu)
+    dxn = ops.gemm(q_dgu, s_dgu, qw.q_gu_t, qw.s_gu_t, scale_a=g_dgu, scale_b=qw.g_gu)
+    del q_dgu, s_dgu
+    # wgrad of W_gu: dgu^T . n(x)
+    q_dgut, s_dgut = ops.quantize_t(dgu, global_scale=g_dgu)
+    del dgu
+    q_xnt, s_xnt = ops.quantize_t(sv.x, global_scale=sv.g_xn, row_scale=sv.inv_rms, gamma=gamma)
+    ops.gemm(q_dgut, s_dgut, q_xnt, s_xnt, scale_a=g_dgu, scale_b=sv.g_xn, out=grad_gu, accumulate=accumulate)
+    del q_dgut, s_dgut, q_xnt, s_xnt
+    dx = ops.rmsnorm_bwd(sv.x, gamma, sv.inv_rms, dxn, dres=dy, dgamma_acc=grad_gamma)
+    return dx
+
+
+# ----------------------------------------------------------------------------
+# autograd front end
+# ----------------------------------------------------------------------------
+
+class NVFP4SwiGLUFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, gamma, w_gu, w_down, eps):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        qw = quantize_weights(w_gu, w_down, need_t=True)
+        y, sv = block_forward(x2, gamma, qw, eps)
+        ctx.qw, ctx.sv = qw, sv
+        ctx.save_for_backward(gamma)
+        ctx.shape = shape
+        return y.reshape(shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        (gamma,) = ctx.saved_tensors
+        dy2 = dy.reshape(-1, ctx.shape[-1]).contiguous().to(torch.bfloat16)
+        d = gamma.numel()
+        grad_gamma = torch.zeros(d, device=dy.device, dtype=torch.float32)
+        grad_gu = torch.empty((ctx.sv.gu.shape[1], d), device=dy.device, dtype=torch.bfloat16)
+        grad_down = torch.empty((d, ctx.sv.h.shape[1]), device=dy.device, dtype=torch.bfloat16)
+        dx = block_backward(dy2, gamma, ctx.qw, ctx.sv, grad_gamma, grad_gu, grad_down, accumulate=False)
+        ctx.qw = ctx.sv = None
+        return dx.reshape(ctx.shape), grad_gamma.to(gamma.dtype), grad_gu, grad_down, None
+
+
+class NVFP4SwiGLUMLP(nn.Module):
+    """Pre-norm residual SwiGLU MLP block with NVFP4 GEMMs in forward and backward."""
+
+    def __init__(self, d_model: int, d_ff: int, eps: float = 1e-6, device=None, dtype=torch.bfloat16,
+                 init_std: float = 0.02):
+        super().__init__()
+        self.d_model, self.d_ff, self.eps = d_model, d_ff, eps
+        self.gamma = nn.Parameter(torch.ones(d_model, device=device, dtype=dtype))
+        self.w_gu = nn.Parameter(torch.empty(2 * d_ff, d_model, device=device, dtype=dtype))
+        self.w_down = nn.Parameter(torch.empty(d_model, d_ff, device=device, dtype=dtype))
+        with torch.no_grad():
+            self.w_gu.normal_(0.0, init_std)
+            self.w_down.normal_(0.0, init_std)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return NVFP4SwiGLUFunction.apply(x, self.gamma, self.w_gu, self.w_down, self.eps)
+
+
+# ----------------------------------------------------------------------------
+# explicit training step for a stack of blocks (no autograd), with DP
+# ----------------------------------------------------------------------------
+
+@dataclass
+class AdamConfig:
+    lr: float = 1e-4
+    beta1: float = 0.9
+    beta2: float = 0.95
+    eps: float = 1e-8
+    weight_decay: float = 0.0
+
+
+class BlockState:
+    """Flat bf16 parameter / gradient buckets and fp32 Adam moments of one block."""
+
+    def __init__(self, d: int, f: int, device, gen: Optional[torch.Generator], init_std: float,
+                 grad_f32: bool):
+        self.d, self.f = d, f
+        n = d + 2 * f * d + d * f
+        self.numel = n
+        self.param = torch.empty(n, device=device, dtype=torch.bfloat16)
+        self.gamma = self.param[:d]
+        self.w_gu = self.param[d:d + 2 * f * d].view(2 * f, d)
+        self.w_down = self.param[d + 2 * f * d:].view(d, f)
+        with torch.no_grad():
+            self.gamma.fill_(1.0)
+            w = torch.empty(2 * f * d + d * f, device=device, dtype=torch.float32)
+            w.normal_(0.0, init_std, generator=gen)
+            self.param[d:].copy_(w)
+            del w
+        # bf16 gradient bucket (the all-reduce payload): gamma | W_gu | W_down
+        self.grad = torch.zeros(n, device=device, dtype=torch.bfloat16)
+        self.grad_gamma32 = torch.zeros(d, device=device, dtype=torch.float32)
+        self.grad_gu = self.grad[d:d + 2 * f * d].view(2 * f, d)
+        self.grad_down = self.grad[d + 2 * f * d:].view(d, f)
+        if grad_f32:   # micro-batch accumulation buffers
+            self.acc_gu = torch.zeros(2 * f, d, device=device, dtype=torch.float32)
+            self.acc_down = torch.zeros(d, f, device=device, dtype=torch.float32)
+        else:
+            self.acc_gu = self.acc_down = None
+        self.m = torch.zeros(n, device=device, dtype=torch.float32)
+        self.v = torch.zeros(n, device=device, dtype=torch.float32)
+
+
+class NVFP4MLPStackTrainer:
+    """Training step of a stack of NVFP4 RMSNorm+SwiGLU blocks.
+
+    One step: forward over all blocks (micro-batched), backward from a given
+    upstream gradient, per-block bf16 gradient all-reduce (NCCL through
+    torch.distributed when a process group is initialised) launched as soon
+    as the block's wgrads are done so it overlaps the backward of the blocks
+    below, then the fp32 AdamW update of every block."""
+
+    def __init__(self, n_blocks: int, d_model: int, d_ff: int, *, device="cuda", seed: int = 0,
+                 micro_tokens: int = 16384, eps: float = 1e-6, adam: Optional[AdamConfig] = None,
+                 init_std: float = 0.02, process_group=None, max_local_tokens: Optional[int] = None):
+        self.device = torch.device(device)
+        self.n_blocks, self.d, self.f = n_blocks, d_model, d_ff
+        self.micro_tokens = micro_tokens
+        self.eps = eps
+        self.adam = adam or AdamConfig()
+        self.pg = process_group
+        gen = torch.Generator(device=self.device).manual_seed(seed)
+        grad_f32 = max_local_tokens is None or max_local_tokens > micro_tokens
+        self.blocks = [BlockState(d_model, d_ff, self.device, gen, init_std, grad_f32) for _ in range(n_blocks)]
+        self.step_count = 0
+        self.world = 1
+        if process_group is not None:
+            import torch.distributed as dist
+            self.world = dist.get_world_size(process_group)
+
+    # -- one optimizer step -------------------------------------------------
+    def step(self, x: torch.Tensor, dy: torch.Tensor) -> torch.Tensor:
+        """x, dy: bf16 [T_local, D] on this rank's device.  Returns a 1-element
+        fp32 tensor (sum of the output, a cheap device-side step result)."""
+        import torch.distributed as dist
+        t = x.shape[0]
+        n_micro = max(1, math.ceil(t / self.micro_tokens))
+        qws = [quantize_weights(b.w_gu, b.w_down, need_t=True) for b in self.blocks]
+        for b in self.blocks:
+            b.grad_gamma32.zero_()
+        out_sum = torch.zeros(1, device=self.device, dtype=torch.float32)
+        works: List = [None] * self.n_blocks
+        for mi in range(n_micro):
+            lo, hi = mi * self.micro_tokens, min(t, (mi + 1) * self.micro_tokens)
+            h = x[lo:hi]
+            saved: List[Saved] = []
+            for bi, b in enumerate(self.blocks):
+                h, sv = block_forward(h, b.gamma, qws[bi], self.eps)
+                saved.append(sv)
+            out_sum += h.sum(dtype=torch.float32)
+            g = dy[lo:hi]
+            last = mi == n_micro - 1
+            for bi in reversed(range(self.n_blocks)):
+                b = self.blocks[bi]
+                if n_micro == 1:
+                    g = block_backward(g, b.gamma, qws[bi], saved[bi], b.grad_gamma32, b.grad_gu, b.grad_down,
+                                       accumulate=False)
+                else:
+                    if mi == 0:
+                        b.acc_gu.zero_()
+                        b.acc_down.zero_()
+                    g = block_backward(g, b.gamma, qws[bi], saved[bi], b.grad_gamma32, b.acc_gu, b.acc_down,
+                                       accumulate=True)
+                    if last:
+                        b.grad_gu.copy_(b.acc_gu)
+                        b.grad_down.copy_(b.acc_down)
+                saved[bi] = None
+                if last:
+                    b.grad[:self.d].copy_(b.grad_gamma32)
+                    if self.pg is not None and self.world > 1:
+                        works[bi] = dist.all_reduce(b.grad, op=dist.ReduceOp.SUM, group=self.pg, async_op=True)
+        self.step_count += 1
+        a = self.adam
+        for bi, b in enumerate(self.blocks):
+            if works[bi] is not None:
+                works[bi].wait()
+            ops.adamw_step(b.param, b.grad, b.m, b.v, lr=a.lr, beta1=a.beta1, beta2=a.beta2, eps=a.eps,
+                           weight_decay=a.weight_decay, step=self.step_count, grad_scale=1.0 / self.world)
+        return out_sum
+
+    def flops_per_step(self, tokens: int) -> float:
+        return 3 * 3 * 2.0 * tokens * self.d * self.f * self.n_blocks
