@@ -33,6 +33,7 @@ import torch
 import torch.nn as nn
 
 from . import ops
+from .dp import BucketAllReducer
 
 
 @dataclass
@@ -232,23 +233,19 @@ class NVFP4MLPStackTrainer:
         grad_f32 = max_local_tokens is None or max_local_tokens > micro_tokens
         self.blocks = [BlockState(d_model, d_ff, self.device, gen, init_std, grad_f32) for _ in range(n_blocks)]
         self.step_count = 0
-        self.world = 1
-        if process_group is not None:
-            import torch.distributed as dist
-            self.world = dist.get_world_size(process_group)
+        self.reducer = BucketAllReducer(process_group) if process_group is not None else None
+        self.world = self.reducer.world if self.reducer is not None else 1
 
     # -- one optimizer step -------------------------------------------------
     def step(self, x: torch.Tensor, dy: torch.Tensor) -> torch.Tensor:
         """x, dy: bf16 [T_local, D] on this rank's device.  Returns a 1-element
         fp32 tensor (sum of the output, a cheap device-side step result)."""
-        import torch.distributed as dist
         t = x.shape[0]
         n_micro = max(1, math.ceil(t / self.micro_tokens))
         qws = [quantize_weights(b.w_gu, b.w_down, need_t=True) for b in self.blocks]
         for b in self.blocks:
             b.grad_gamma32.zero_()
         out_sum = torch.zeros(1, device=self.device, dtype=torch.float32)
-        works: List = [None] * self.n_blocks
         for mi in range(n_micro):
             lo, hi = mi * self.micro_tokens, min(t, (mi + 1) * self.micro_tokens)
             h = x[lo:hi]
@@ -276,13 +273,13 @@ class NVFP4MLPStackTrainer:
                 saved[bi] = None
                 if last:
                     b.grad[:self.d].copy_(b.grad_gamma32)
-                    if self.pg is not None and self.world > 1:
-                        works[bi] = dist.all_reduce(b.grad, op=dist.ReduceOp.SUM, group=self.pg, async_op=True)
+                    if self.reducer is not None:
+                        self.reducer.launch(bi, b.grad)
         self.step_count += 1
         a = self.adam
         for bi, b in enumerate(self.blocks):
-            if works[bi] is not None:
-                works[bi].wait()
+            if self.reducer is not None:
+                self.reducer.wait(bi)
             ops.adamw_step(b.param, b.grad, b.m, b.v, lr=a.lr, beta1=a.beta1, beta2=a.beta2, eps=a.eps,
                            weight_decay=a.weight_decay, step=self.step_count, grad_scale=1.0 / self.world)
         return out_sum

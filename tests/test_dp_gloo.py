@@ -1,0 +1,122 @@
+"""Data-parallel host logic on CPU with world_size-2 gloo process groups:
+bucketed async all-reduce, mean-gradient scaling, and host-side failure
+detection (a rank that dies before the collective)."""
+import datetime
+import os
+import socket
+import sys
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _init(rank, world, port, timeout_s):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _dp_module():
+    sys.path.insert(0, ROOT)
+    import __graft_entry__
+    pkg = __graft_entry__.import_package()
+    import importlib
+    return importlib.import_module("nvfp4_b200.dp")
+
+
+def _worker_reduce(rank, world, port, q):
+    try:
+        _init(rank, world, port, 30)
+        dp = _dp_module()
+        red = dp.BucketAllReducer(dist.group.WORLD)
+        assert red.active and red.world == world
+        buckets = {i: torch.full((1000 + i,), float(rank + 1) * (i + 1)) for i in range(4)}
+        for i in reversed(range(4)):          # backward order: last block first
+            red.launch(i, buckets[i])
+        with pytest.raises(RuntimeError):
+            red.launch(0, buckets[0])          # same bucket twice in flight
+        for i in range(4):
+            red.wait(i)
+        expect = sum(r + 1 for r in range(world))
+        for i in range(4):
+            assert torch.allclose(buckets[i], torch.full_like(buckets[i], expect * (i + 1)))
+            assert torch.allclose(buckets[i] * red.grad_scale(), torch.full_like(buckets[i], expect * (i + 1) / world))
+        red.wait_all()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
+def _worker_failure(rank, world, port, q):
+    try:
+        _init(rank, world, port, 4)
+        dp = _dp_module()
+        red = dp.BucketAllReducer(dist.group.WORLD)
+        if rank == 1:
+            q.put((rank, "exiting"))
+            q.close()
+            q.join_thread()                  # flush the message before dying
+            os._exit(3)                      # the failing rank dies between steps
+        t = torch.ones(16)
+        try:
+            red.launch("blk", t)
+            red.wait("blk", timeout_s=5)
+            q.put((rank, "no error"))
+        except Exception as e:               # detected on the host: connection closed / timeout
+            q.put((rank, f"detected:{type(e).__name__}"))
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
+def _run(target, world=2, timeout=60):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    for _ in range(world):
+        r, msg = q.get(timeout=timeout)
+        out[r] = msg
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    return out
+
+
+def test_bucketed_allreduce_two_ranks():
+    out = _run(_worker_reduce)
+    assert out == {0: "ok", 1: "ok"}, out
+
+
+def test_rank_failure_is_detected_on_host():
+    out = _run(_worker_failure)
+    assert out[1] == "exiting"
+    assert out[0].startswith("detected:"), out[0]
+
+
+def test_single_process_reducer_is_noop():
+    dp = _dp_module()
+    red = dp.BucketAllReducer(None)
+    assert not red.active and red.grad_scale() == 1.0
+    t = torch.ones(4)
+    red.launch(0, t)
+    red.wait(0)
+    assert torch.equal(t, torch.ones(4))

@@ -1,0 +1,132 @@
+"""GPU parity of the NVFP4 SwiGLU MLP block (forward, dgrad, wgrad) against the
+oracle's dequantize -> float64 matmul emulation.  Tolerance: relative
+Frobenius error <= 1e-2 on every bf16 output (intermediate bf16 rounding may
+flip single nibbles downstream; the stated bar absorbs that)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import mlp_oracle, nvfp4_oracle as orc
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+def f32(t):
+    return t.detach().float().cpu().numpy()
+
+
+def test_block_forward_backward_matches_emulation(pkg):
+    import importlib
+    mlp = importlib.import_module("nvfp4_b200.mlp")
+    t, d, f = 256, 256, 512
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(t, d, device="cuda", generator=g).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(d, device="cuda", generator=g)).to(torch.bfloat16)
+    w_gu = (0.02 * torch.randn(2 * f, d, device="cuda", generator=g)).to(torch.bfloat16)
+    w_down = (0.02 * torch.randn(d, f, device="cuda", generator=g)).to(torch.bfloat16)
+    dy = (1e-3 * torch.randn(t, d, device="cuda", generator=g)).to(torch.bfloat16)
+    qw = mlp.quantize_weights(w_gu, w_down)
+    y, sv = mlp.block_forward(x, gamma, qw)
+    gg = torch.zeros(d, device="cuda")
+    dgu = torch.empty(2 * f, d, device="cuda", dtype=torch.bfloat16)
+    dd = torch.empty(d, f, device="cuda", dtype=torch.bfloat16)
+    dx = mlp.block_backward(dy, gamma, qw, sv, gg, dgu, dd, accumulate=False)
+    torch.cuda.synchronize()
+    assert pkg.ops.device_error() == 0
+
+    inv = sv.inv_rms.cpu().numpy()
+    ey, esv = mlp_oracle.block_forward(f32(x), f32(gamma), f32(w_gu), f32(w_down), inv)
+    assert orc.rel_frobenius(f32(y), ey) < TOL
+    assert orc.rel_frobenius(f32(sv.gu), esv["gu"]) < TOL
+    edx, edg, edgu, edd = mlp_oracle.block_backward(f32(dy), f32(x), f32(gamma), f32(w_gu), f32(w_down), inv, esv)
+    assert orc.rel_frobenius(f32(dx), edx) < TOL
+    assert orc.rel_frobenius(f32(dd), edd) < 2 * TOL
+    assert orc.rel_frobenius(f32(dgu), edgu) < 2 * TOL
+    assert orc.rel_frobenius(gg.cpu().numpy(), edg) < 2 * TOL
+
+
+def test_autograd_module_close_to_bf16_reference(pkg):
+    """NVFP4 module vs an unquantized torch fp32 computation of the same block:
+    NVFP4 error is ~5-15% relative; gradients must point the same way."""
+    import importlib
+    mlp = importlib.import_module("nvfp4_b200.mlp")
+    torch.manual_seed(0)
+    m = mlp.NVFP4SwiGLUMLP(256, 512, device="cuda")
+    x = torch.randn(128, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    y = m(x)
+    dy = torch.randn_like(y) * 1e-2
+    y.backward(dy)
+    xr = x.detach().float().requires_grad_(True)
+    gam = m.gamma.detach().float().requires_grad_(True)
+    wgu = m.w_gu.detach().float().requires_grad_(True)
+    wd = m.w_down.detach().float().requires_grad_(True)
+    xn = xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-6) * gam
+    gu = xn @ wgu.T
+    gate, up = gu.chunk(2, dim=-1)
+    yr = xr + (torch.nn.functional.silu(gate) * up) @ wd.T
+    yr.backward(dy.float())
+    rel = lambda a, b: ((a.float() - b).norm() / b.norm()).item()
+    assert rel(y.detach(), yr.detach()) < 0.05
+    assert rel(x.grad, xr.grad) < 0.3
+    assert rel(m.w_down.grad, wd.grad) < 0.3
+    assert rel(m.w_gu.grad, wgu.grad) < 0.3
+    cos = torch.nn.functional.cosine_similarity(m.w_gu.grad.float().flatten(), wgu.grad.flatten(), dim=0)
+    assert cos.item() > 0.95
+
+
+def test_stack_trainer_microbatch_accumulation_is_exact_sum(pkg):
+    """Two micro-batches accumulate fp32 wgrads: the bucket must equal the sum of
+    the two micro-batch gradients computed separately (same weights, same
+    per-micro-batch scales), up to the final bf16 rounding."""
+    import importlib
+    mlp = importlib.import_module("nvfp4_b200.mlp")
+    t, d, f = 512, 256, 512
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randn(t, d, device="cuda", generator=g).to(torch.bfloat16)
+    dy = (1e-3 * torch.randn(t, d, device="cuda", generator=g)).to(torch.bfloat16)
+    tr = mlp.NVFP4MLPStackTrainer(1, d, f, seed=7, micro_tokens=256, max_local_tokens=t)
+    blk = tr.blocks[0]
+    p0 = blk.param.clone()
+    qw = mlp.quantize_weights(blk.w_gu, blk.w_down)
+    acc_gu = torch.zeros(2 * f, d, device="cuda")
+    acc_dn = torch.zeros(d, f, device="cuda")
+    acc_gam = torch.zeros(d, device="cuda")
+    for lo in (0, 256):
+        y, sv = mlp.block_forward(x[lo:lo + 256], blk.gamma, qw)
+        ggu = torch.empty(2 * f, d, device="cuda")
+        gdn = torch.empty(d, f, device="cuda")
+        mlp.block_backward(dy[lo:lo + 256], blk.gamma, qw, sv, acc_gam, ggu, gdn, accumulate=False)
+        acc_gu += ggu
+        acc_dn += gdn
+    r = tr.step(x, dy)
+    torch.cuda.synchronize()
+    assert torch.isfinite(r).all()
+    rel = lambda a, b: ((a.float() - b).norm() / b.norm()).item()
+    assert rel(blk.grad_gu, acc_gu) < 1e-2
+    assert rel(blk.grad_down, acc_dn) < 1e-2
+    assert rel(blk.grad[:d], acc_gam) < 1e-2
+    # AdamW moved the parameters by at most ~lr per element
+    delta = (blk.param.float() - p0.float()).abs()
+    assert 0 < delta.max().item() < 1e-2
+    assert pkg.ops.device_error() == 0
+
+
+def test_stack_trainer_full_batch_vs_microbatch_consistent(pkg):
+    """Full-batch and micro-batched steps estimate the same gradient: NVFP4
+    noise differs (per-micro-batch global scales), direction must agree."""
+    import importlib
+    mlp = importlib.import_module("nvfp4_b200.mlp")
+    t, d, f = 512, 256, 512
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randn(t, d, device="cuda", generator=g).to(torch.bfloat16)
+    dy = (1e-3 * torch.randn(t, d, device="cuda", generator=g)).to(torch.bfloat16)
+    a = mlp.NVFP4MLPStackTrainer(2, d, f, seed=7, micro_tokens=512, max_local_tokens=t)
+    b = mlp.NVFP4MLPStackTrainer(2, d, f, seed=7, micro_tokens=256, max_local_tokens=t)
+    assert torch.equal(a.blocks[0].param, b.blocks[0].param)
+    a.step(x, dy)
+    b.step(x, dy)
+    for ba, bb in zip(a.blocks, b.blocks):
+        ga, gb = ba.grad.float(), bb.grad.float()
+        assert ((ga - gb).norm() / ga.norm()).item() < 0.3
+        assert torch.nn.functional.cosine_similarity(ga, gb, dim=0).item() > 0.95
