@@ -1,29 +1,41 @@
-// NVFP4 block-scaled GEMM for B200: tcgen05.mma kind::mxf4nvf4 (scale_vec::4X,
-// E4M3 scales per 1x16 block), TMA-fed, TMEM accumulators, warp-specialised
-// persistent kernel.
+// NVFP4 block-scaled GEMM for B200: tcgen05.mma.cta_group::2 kind::mxf4nvf4
+// (scale_vec::4X, E4M3 scale per 1x16 block), TMA-fed, TMEM accumulators,
+// warp-specialised persistent kernel on CTA pairs.
 //
-//   D[m, n] = epilogue(alpha * sum_k A[m,k] * B[n,k] + bias[n])
+//   D[m, n] = epilogue(alpha * sum_k A[m,k] * B[n,k] + bias[n]) + residual[m, n]
 //
 // Contract of the reference op gn_kernels::cutlass_sm120a_nvfp4_mm
 // (cutlass_mm_fp4.cu:167-272): A packed E2M1 [m, k/2] row-major, B packed
 // [n, k/2] (the reference's column-major B), scales in the 128x4-atom
 // swizzled layout, scalar output scale, optional bf16 bias, bf16 output.
 //
-// Structure (one CTA per SM, 192 threads):
-//   warp 0      TMA producer: A tile 128x256 (SW128), B tile 256x256 (SW128)
-//               and the scale atoms (plain bulk copies: the swizzled global
-//               layout already is the tcgen05 scale-atom layout, so a
-//               128-row x 256-k scale slab is 2 KB contiguous).
-//   warp 1      TMEM allocator + MMA issuer: per stage, tcgen05.cp moves the
-//               scale atoms into TMEM (32x128b.warpx4: each 512-byte atom
-//               fills 4 columns across all 128 lanes), then 4 MMAs
-//               128x256x64 accumulate into TMEM columns [0, 256).
-//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, scale, bias,
-//               activation, convert and store; the accumulator is released
-//               as soon as the last column block is in registers.
+// Structure: clusters of 2 CTAs (one per SM) own 256x256 output tiles.
+//   CTA r of the pair holds A rows [128r, 128r+128) and B rows
+//   [128r, 128r+128) of the tile in shared memory, its own 128 rows of A's
+//   scales and all 256 rows of B's scales; each CTA's TMEM accumulates its
+//   128 x 256 half of the tile.
+//   warp 0      TMA producer (both CTAs): A, B (128B swizzle) and the scale
+//               slabs (the swizzled global scale layout already is the
+//               tcgen05 scale-atom layout: a 128-row x 256-k slab is 2 KB
+//               contiguous, loaded as a 2-D box over 256-byte rows).  All
+//               loads signal the leader CTA's stage barrier.
+//   warp 10     scale copier (leader CTA): tcgen05.cp.cta_group::2 moves each
+//               scale atom into both CTAs' TMEM (32x128b.warpx4: 4 columns x
+//               128 lanes) into a per-stage ring slot and commits to a
+//               "scales ready" barrier.  Issued from its own thread, the copies
+//               for later stages overlap the MMAs of earlier ones (a single
+//               issuing thread's copies and MMAs execute strictly in order).
+//   warp 1      TMEM allocator (both CTAs) and, in the leader CTA, the MMA
+//               issuer: 4 MMAs 256x256x64 per 256-k stage; tcgen05.commit
+//               multicasts stage release / accumulator-ready to both CTAs.
+//   warps 2-9   epilogue (both CTAs): two warps per TMEM lane quadrant, each
+//               drains 128 columns in two 64-column rounds, releases the
+//               accumulator to the leader's MMA warp, then stores, so the
+//               stores overlap the next tile's main loop.
 // Every mbarrier wait is bounded: on timeout the CTA records
 // NVFP4B200_ERR_TIMEOUT in a device error word, drains what it issued and
-// returns, so a broken pipeline cannot hang the GPU.
+// returns, so a broken pipeline cannot hang the GPU.  No TMA load uses
+// cluster multicast.
 #include "common.cuh"
 
 #include <cuda.h>
@@ -36,38 +48,44 @@ __device__ int g_device_error = 0;
 
 namespace gemm {
 
-constexpr int BM = 128, BN = 256, BK = 256;   // BK counts fp4 elements
-constexpr int BK_BYTES = BK / 2;              // 128 bytes: one SW128 row
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK_BYTES;        // 16 KB
-constexpr int B_BYTES = BN * BK_BYTES;        // 32 KB
-constexpr int SFA_BYTES = BM * (BK / 16);     // 2 KB = 4 atoms
-constexpr int SFB_BYTES = BN * (BK / 16);     // 4 KB = 2 row groups x 4 atoms
-constexpr int NUM_THREADS = 192;
+constexpr int TILE_M = 256, TILE_N = 256, BK = 256;  // pair tile; BK counts fp4 elements
+constexpr int CTA_M = 128, CTA_N = 128;               // rows of A / B held by one CTA
+constexpr int BK_BYTES = BK / 2;                      // 128 bytes: one SW128 row
+constexpr int STAGES = 5;
+constexpr int A_BYTES = CTA_M * BK_BYTES;             // 16 KB
+constexpr int B_BYTES = CTA_N * BK_BYTES;             // 16 KB
+constexpr int SFA_BYTES = 2048;                       // 128 rows x 16 scales = 4 atoms
+constexpr int SFB_BYTES = 4096;                       // 2 row groups x 4 atoms
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+constexpr uint32_t STAGE_TX = 2u * STAGE_BYTES;       // bytes landing per stage across the pair
+constexpr int EPI_WARPS = 8;
+constexpr int COPIER_WARP = 2 + EPI_WARPS;
+constexpr int NUM_THREADS = 32 * (COPIER_WARP + 1);
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;
-constexpr int SFA_COL = 256;                  // 4 MMAs x 4 columns
-constexpr int SFB_COL = 272;                  // 4 MMAs x 8 columns
-constexpr int NUM_BARS = 2 * STAGES + 3;
-constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES) + 1024 + 256;
+// Scale columns: a ring with one slot per pipeline stage (A: 4 MMAs x 4
+// columns, B: 4 MMAs x 8 columns), so copies run ahead of the MMAs.
+constexpr int SF_COL0 = 256;
+constexpr int SF_SLOT_COLS = 48;
+static_assert(SF_COL0 + STAGES * SF_SLOT_COLS <= TMEM_COLS, "TMEM columns");
+constexpr int NUM_BARS = 3 * STAGES + 3;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;  // about 2 s at 2 GHz
-constexpr int GROUP_M = 16;                   // tile raster: 16 m-tiles per group
+constexpr int GROUP_M = 8;                            // raster: 8 pair-rows (2048 rows) per group
 
 // Instruction descriptor (kind::mxf4nvf4): A/B E2M1 (=1), K-major, E4M3
-// scales, N>>3 at bit 17, M>>4 at bit 24, dense K=64.
-constexpr uint32_t IDESC = (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// scales, N>>3 at bit 17, M>>4 at bit 24 (M = 256 across the CTA pair), K=64.
+constexpr uint32_t IDESC =
+    (1u << 7) | (1u << 10) | ((uint32_t)(TILE_N >> 3) << 17) | ((uint32_t)(TILE_M >> 4) << 24);
 
 struct Params {
-  const uint8_t* sfa;
-  const uint8_t* sfb;
   const float* scale_a;
   const float* scale_b;
   const uint16_t* bias;
-  const uint16_t* residual;   // bf16 [m, n] with row stride ldd, added after bias
+  const uint16_t* residual;  // bf16 [m, n], row stride ldd, added after the activation
   void* d;
   int64_t m, n, k, ldd;
-  int64_t sf_atoms;       // scale atoms per 128-row group = ceil(k/64)
-  int64_t sfb_groups;     // 128-row groups of B's scale tensor
+  int64_t sf_atoms;          // scale atoms per 128-row group = ceil(k/64)
   int num_m_tiles, num_n_tiles, num_k_tiles;
   int d_f32, accumulate, epilogue;
 };
@@ -76,8 +94,19 @@ struct Params {
 // PTX wrappers
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -85,8 +114,8 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -99,13 +128,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Same, with cluster-scope acquire: for barriers that the peer CTA signals.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait for the phase with the given parity to complete.  Returns
 // false when the CTA-wide abort flag is raised or the limit expires.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
+  auto try_once = [&]() { return CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity); };
+  if (try_once()) return true;
   const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (try_once()) return true;
     if ((it & 63) == 0) {
       if (*abort_flag) return false;
       if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
@@ -117,50 +160,58 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag) {
   atomicExch(&g_device_error, NVFP4B200_ERR_TIMEOUT);
 }
 
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+// 2-D tiled TMA load into this CTA's shared memory; completion bytes are
+// counted on `bar`, which may be the pair leader's barrier (.cta_group::2).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(map), "r"(bar), "r"(x), "r"(y)
       : "memory");
-}
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(bar)
-               : "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
-__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+__device__ __forceinline__ void tmem_alloc2(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
                : "memory");
 }
-__device__ __forceinline__ void tmem_relinquish() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+__device__ __forceinline__ void tmem_relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+// Arrive once on `bar` (same shared-memory offset) in both CTAs of the pair
+// when all prior tcgen05 operations of this thread have completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
 }
-__device__ __forceinline__ void tc_cp_scales(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+// Arrive once on `bar` in this CTA when this thread's prior tcgen05 pair operations complete.
+__device__ __forceinline__ void tc_commit_local(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t sfa, uint32_t sfb,
-                                       uint32_t accumulate) {
+__device__ __forceinline__ void tc_cp_scales_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+__device__ __forceinline__ void tc_mma_pair(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t sfa, uint32_t sfb,
+                                            uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(d),
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+          d),
       "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate), "r"(sfa), "r"(sfb)
       : "memory");
 }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -214,12 +265,73 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// 64 accumulator columns [c0, c0+64) of this thread's row -> final values,
+// in place (float bits in `v`): scale, bias, activation, residual.
+__device__ __forceinline__ void finish64(uint32_t* v, const Params& p, float alpha, int64_t row, int64_t col0,
+                                         bool row_ok) {
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+  if (p.bias) {
+#pragma unroll
+    for (int i8 = 0; i8 < 8; ++i8) {
+      if (col0 + 8 * i8 < p.n) {
+        const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + col0 + 8 * i8));
+        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[8 * i8 + 2 * j] = __float_as_uint(__uint_as_float(v[8 * i8 + 2 * j]) + bf16lo(bw[j]));
+          v[8 * i8 + 2 * j + 1] = __float_as_uint(__uint_as_float(v[8 * i8 + 2 * j + 1]) + bf16hi(bw[j]));
+        }
+      }
+    }
+  }
+  if (p.epilogue != NVFP4B200_EPI_NONE) {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = __float_as_uint(apply_epi(__uint_as_float(v[i]), p.epilogue));
+  }
+  if (p.residual && row_ok) {
+    const uint16_t* res = p.residual + row * p.ldd + col0;
+#pragma unroll
+    for (int i8 = 0; i8 < 8; ++i8) {
+      if (col0 + 8 * i8 < p.n) {
+        const uint4 rv = *reinterpret_cast<const uint4*>(res + 8 * i8);
+        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[8 * i8 + 2 * j] = __float_as_uint(__uint_as_float(v[8 * i8 + 2 * j]) + bf16lo(rw[j]));
+          v[8 * i8 + 2 * j + 1] = __float_as_uint(__uint_as_float(v[8 * i8 + 2 * j + 1]) + bf16hi(rw[j]));
+        }
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void store_f32_64(const uint32_t* v, const Params& p, int64_t row, int64_t col0) {
+  float* dst = static_cast<float*>(p.d) + row * p.ldd + col0;
+#pragma unroll
+  for (int i4 = 0; i4 < 16; ++i4) {
+    if (col0 + 4 * i4 < p.n) {
+      float4 o = make_float4(__uint_as_float(v[4 * i4]), __uint_as_float(v[4 * i4 + 1]),
+                             __uint_as_float(v[4 * i4 + 2]), __uint_as_float(v[4 * i4 + 3]));
+      if (p.accumulate) {
+        const float4 old = reinterpret_cast<const float4*>(dst)[i4];
+        o.x += old.x;
+        o.y += old.y;
+        o.z += old.z;
+        o.w += old.w;
+      }
+      reinterpret_cast<float4*>(dst)[i4] = o;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                      const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
                       const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -232,64 +344,78 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  auto full_bar = [&](int s) { return smem_u32(bars + s); };
-  auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
-  const uint32_t tmem_full_bar = smem_u32(bars + 2 * STAGES);
-  const uint32_t tmem_empty_bar = smem_u32(bars + 2 * STAGES + 1);
-  const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 2);
+  const uint32_t rank = cluster_rank();          // 0 = leader (issues the MMAs)
+  const bool leader = rank == 0;
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };             // leader: all bytes of the stage landed
+  auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };    // both: MMAs done with the stage
+  auto sf_ready_bar = [&](int s) { return smem_u32(bars + 2 * STAGES + s); };  // leader: scales in TMEM
+  const uint32_t tmem_full_bar = smem_u32(bars + 3 * STAGES);
+  const uint32_t tmem_empty_bar = smem_u32(bars + 3 * STAGES + 1);
+  const uint32_t drain_bar = smem_u32(bars + 3 * STAGES + 2);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
+      mbar_init(sf_ready_bar(s), 1);
     }
     mbar_init(tmem_full_bar, 1);
-    mbar_init(tmem_empty_bar, 4);
+    mbar_init(tmem_empty_bar, 2 * EPI_WARPS);
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
+    prefetch_tmap(&tmap_sfa);
+    prefetch_tmap(&tmap_sfb);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc2(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish2();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   const int total_tiles = p.num_m_tiles * p.num_n_tiles;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer (both CTAs) ----------------
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int armed_phase[STAGES];
       for (int s = 0; s < STAGES; ++s) armed_phase[s] = -1;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+      for (int tile = cluster_id; ok && tile < total_tiles; tile += num_clusters) {
         int mb, nb;
         tile_coords(tile, p, mb, nb);
-        const int ngroups_b = (2 * nb + 1 < p.sfb_groups) ? 2 : 1;
+        const int a_row = mb * TILE_M + (int)rank * CTA_M;
+        const int b_row = nb * TILE_N + (int)rank * CTA_N;
+        const int sfa_group = 2 * mb + (int)rank;
         for (int kt = 0; kt < p.num_k_tiles; ++kt) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag)) {
             ok = false;
             break;
           }
-          const int nkb = kblocks_in_tile(p, kt);
-          const uint32_t sf_bytes = (uint32_t)nkb * 512u;
-          mbar_expect_tx(full_bar(stage), A_BYTES + B_BYTES + sf_bytes * (1 + ngroups_b));
-          armed_phase[stage] = (int)phase;
-          tma_load_2d(smem_u32(sA + stage * A_BYTES), &tmap_a, full_bar(stage), kt * BK_BYTES, mb * BM);
-          tma_load_2d(smem_u32(sB + stage * B_BYTES), &tmap_b, full_bar(stage), kt * BK_BYTES, nb * BN);
-          bulk_load(smem_u32(sSFA + stage * SFA_BYTES), p.sfa + ((int64_t)mb * p.sf_atoms + (int64_t)kt * 4) * 512,
-                    sf_bytes, full_bar(stage));
-          for (int g = 0; g < ngroups_b; ++g)
-            bulk_load(smem_u32(sSFB + stage * SFB_BYTES + g * 2048),
-                      p.sfb + ((int64_t)(2 * nb + g) * p.sf_atoms + (int64_t)kt * 4) * 512, sf_bytes, full_bar(stage));
+          const uint32_t lbar = map_to_rank(full_bar(stage), 0);
+          if (leader) {
+            mbar_expect_tx(full_bar(stage), STAGE_TX);
+            armed_phase[stage] = (int)phase;
+          }
+          tma_load_2d_pair(smem_u32(sA + stage * A_BYTES), &tmap_a, lbar, kt * BK_BYTES, a_row);
+          tma_load_2d_pair(smem_u32(sB + stage * B_BYTES), &tmap_b, lbar, kt * BK_BYTES, b_row);
+          // scale slabs: rows of 256 bytes; slab (group, kt) starts at row (group*atoms + 4*kt)*2
+          tma_load_2d_pair(smem_u32(sSFA + stage * SFA_BYTES), &tmap_sfa, lbar, 0,
+                           (int)(((int64_t)sfa_group * p.sf_atoms + 4 * kt) * 2));
+          tma_load_2d_pair(smem_u32(sSFB + stage * SFB_BYTES), &tmap_sfb, lbar, 0,
+                           (int)(((int64_t)(2 * nb) * p.sf_atoms + 4 * kt) * 2));
+          tma_load_2d_pair(smem_u32(sSFB + stage * SFB_BYTES + 2048), &tmap_sfb, lbar, 0,
+                           (int)(((int64_t)(2 * nb + 1) * p.sf_atoms + 4 * kt) * 2));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -298,65 +424,103 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (!ok) {
         raise_abort(abort_flag);
-        // wait (bounded) for the copies this thread issued before returning
-        const long long t0 = clock64();
-        for (int s = 0; s < STAGES; ++s) {
-          if (armed_phase[s] < 0) continue;
-          while (!mbar_try_wait(full_bar(s), (uint32_t)armed_phase[s]) && clock64() - t0 < WAIT_LIMIT_CYCLES) {
+        if (leader) {  // the leader's stage barriers count both CTAs' copies
+          const long long t0 = clock64();
+          for (int s = 0; s < STAGES; ++s) {
+            if (armed_phase[s] < 0) continue;
+            while (!mbar_try_wait(full_bar(s), (uint32_t)armed_phase[s]) && clock64() - t0 < WAIT_LIMIT_CYCLES) {
+            }
           }
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer (leader CTA) ----------------
+    if (leader && lane == 0) {
       int stage = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true, issued = false;
       const uint32_t acc = tmem_base + ACC_COL;
-      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
-        if (!mbar_wait(tmem_empty_bar, acc_phase ^ 1, abort_flag)) {
+      for (int tile = cluster_id; ok && tile < total_tiles; tile += num_clusters) {
+        if (!mbar_wait<true>(tmem_empty_bar, acc_phase ^ 1, abort_flag)) {
           ok = false;
           break;
         }
         acc_phase ^= 1;
         tc_fence_after();
         for (int kt = 0; kt < p.num_k_tiles; ++kt) {
-          if (!mbar_wait(full_bar(stage), phase, abort_flag)) {
+          // scales of this stage are in TMEM (which implies its operands landed)
+          if (!mbar_wait(sf_ready_bar(stage), phase, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const int nkb = kblocks_in_tile(p, kt);
-          const uint32_t a_s = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_s = smem_u32(sB + stage * B_BYTES);
-          const uint32_t sfa_s = smem_u32(sSFA + stage * SFA_BYTES);
-          const uint32_t sfb_s = smem_u32(sSFB + stage * SFB_BYTES);
-          for (int j = 0; j < nkb; ++j) {
-            tc_cp_scales(tmem_base + SFA_COL + 4 * j, desc_scales(sfa_s + 512 * j));
-            tc_cp_scales(tmem_base + SFB_COL + 8 * j, desc_scales(sfb_s + 512 * j));
-            tc_cp_scales(tmem_base + SFB_COL + 8 * j + 4, desc_scales(sfb_s + 2048 + 512 * j));
-          }
-          const uint64_t adesc = desc_sw128(a_s), bdesc = desc_sw128(b_s);
+          const uint32_t sfa_t = tmem_base + SF_COL0 + SF_SLOT_COLS * stage;
+          const uint32_t sfb_t = sfa_t + 16;
+          const uint64_t adesc = desc_sw128(smem_u32(sA + stage * A_BYTES));
+          const uint64_t bdesc = desc_sw128(smem_u32(sB + stage * B_BYTES));
           for (int j = 0; j < nkb; ++j) {
             // advance 32 bytes (64 fp4) along K inside the swizzled 128-byte row
-            tc_mma(acc, adesc + 2 * j, bdesc + 2 * j, tmem_base + SFA_COL + 4 * j, tmem_base + SFB_COL + 8 * j,
-                   (kt | j) != 0);
+            tc_mma_pair(acc, adesc + 2 * j, bdesc + 2 * j, sfa_t + 4 * j, sfb_t + 8 * j, (kt | j) != 0);
           }
           issued = true;
-          tc_commit(empty_bar(stage));
+          tc_commit_pair(empty_bar(stage));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        tc_commit(tmem_full_bar);
+        tc_commit_pair(tmem_full_bar);
       }
       if (!ok) {
         raise_abort(abort_flag);
         if (issued) {
-          tc_commit(drain_bar);
+          tc_commit_pair(drain_bar);
+          const long long t0 = clock64();
+          while (!mbar_try_wait(drain_bar, 0) && clock64() - t0 < WAIT_LIMIT_CYCLES) {
+          }
+        }
+      }
+    }
+  } else if (warp == COPIER_WARP) {
+    // ---------------- scale copier (leader CTA) ----------------
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true, issued = false;
+      for (int tile = cluster_id; ok && tile < total_tiles; tile += num_clusters) {
+        for (int kt = 0; kt < p.num_k_tiles; ++kt) {
+          // operands and scale atoms of both CTAs landed; the slot's previous MMAs are
+          // done (the producer refilled the stage only after they released it)
+          if (!mbar_wait<true>(full_bar(stage), phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int nkb = kblocks_in_tile(p, kt);
+          const uint32_t sfa_s = smem_u32(sSFA + stage * SFA_BYTES);
+          const uint32_t sfb_s = smem_u32(sSFB + stage * SFB_BYTES);
+          const uint32_t sfa_t = tmem_base + SF_COL0 + SF_SLOT_COLS * stage;
+          const uint32_t sfb_t = sfa_t + 16;
+          for (int j = 0; j < nkb; ++j) {
+            tc_cp_scales_pair(sfa_t + 4 * j, desc_scales(sfa_s + 512 * j));
+            tc_cp_scales_pair(sfb_t + 8 * j, desc_scales(sfb_s + 512 * j));
+            tc_cp_scales_pair(sfb_t + 8 * j + 4, desc_scales(sfb_s + 2048 + 512 * j));
+          }
+          issued = true;
+          tc_commit_local(sf_ready_bar(stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        raise_abort(abort_flag);
+        if (issued) {
+          tc_commit_local(drain_bar);
           const long long t0 = clock64();
           while (!mbar_try_wait(drain_bar, 0) && clock64() - t0 < WAIT_LIMIT_CYCLES) {
           }
@@ -364,11 +528,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int quad = warp & 3;  // TMEM lanes this warp may access: [32*quad, 32*quad+32)
+    // ---------------- epilogue (warps 2..9, both CTAs) ----------------
+    const int quad = warp & 3;               // TMEM lanes [32*quad, 32*quad+32)
+    const int half = (warp - 2) >> 2;        // accumulator columns [128*half, 128*half+128)
+    const uint32_t leader_empty = map_to_rank(tmem_empty_bar, 0);
     const float alpha = (p.scale_a ? *p.scale_a : 1.0f) * (p.scale_b ? *p.scale_b : 1.0f);
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+    for (int tile = cluster_id; tile < total_tiles; tile += num_clusters) {
       int mb, nb;
       tile_coords(tile, p, mb, nb);
       bool ok = mbar_wait(tmem_full_bar, acc_phase, abort_flag);
@@ -379,80 +545,52 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       acc_phase ^= 1;
       tc_fence_after();
-      const int64_t row = (int64_t)mb * BM + quad * 32 + lane;
+      const int64_t row = (int64_t)mb * TILE_M + (int64_t)rank * CTA_M + quad * 32 + lane;
       const bool row_ok = row < p.m;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        __syncwarp();  // tcgen05.ld is .sync.aligned: reconverge after the guarded stores
-        tmem_ld32(tmem_base + ACC_COL + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 32), r);
-        tmem_ld_wait();
-        if (c == BN / 32 - 1) {
-          tc_fence_before();
+      const int64_t colbase = (int64_t)nb * TILE_N + half * 128;
+      const uint32_t tbase = tmem_base + ACC_COL + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * 128);
+      if (!p.d_f32) {
+        uint16_t* dst = static_cast<uint16_t*>(p.d) + row * p.ldd + colbase;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          uint32_t acc[64];
           __syncwarp();
-          if (lane == 0) mbar_arrive(tmem_empty_bar);
-        }
-        const int64_t col0 = (int64_t)nb * BN + c * 32;
-        if (!row_ok || col0 >= p.n) continue;
-        float v[32];
+          tmem_ld32(tbase + r * 64, acc);
+          tmem_ld32(tbase + r * 64 + 32, acc + 32);
+          tmem_ld_wait();
+          if (r == 1) {  // every accumulator column of this warp is in registers: release TMEM
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(leader_empty);
+          }
+          finish64(acc, p, alpha, row, colbase + r * 64, row_ok);
+          if (row_ok) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
-        if (p.bias) {
-#pragma unroll
-          for (int i8 = 0; i8 < 4; ++i8) {
-            if (col0 + 8 * i8 >= p.n) break;
-            const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + col0 + 8 * i8));
-            const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              v[8 * i8 + 2 * j] += bf16lo(bw[j]);
-              v[8 * i8 + 2 * j + 1] += bf16hi(bw[j]);
+            for (int i8 = 0; i8 < 8; ++i8) {
+              if (colbase + r * 64 + 8 * i8 < p.n)
+                reinterpret_cast<uint4*>(dst + r * 64)[i8] = make_uint4(
+                    pack_bf16x2(__uint_as_float(acc[8 * i8 + 0]), __uint_as_float(acc[8 * i8 + 1])),
+                    pack_bf16x2(__uint_as_float(acc[8 * i8 + 2]), __uint_as_float(acc[8 * i8 + 3])),
+                    pack_bf16x2(__uint_as_float(acc[8 * i8 + 4]), __uint_as_float(acc[8 * i8 + 5])),
+                    pack_bf16x2(__uint_as_float(acc[8 * i8 + 6]), __uint_as_float(acc[8 * i8 + 7])));
             }
           }
         }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = apply_epi(v[i], p.epilogue);
-        if (p.residual) {
-          const uint16_t* res = p.residual + row * p.ldd + col0;
-#pragma unroll
-          for (int i8 = 0; i8 < 4; ++i8) {
-            if (col0 + 8 * i8 >= p.n) break;
-            const uint4 rv = *reinterpret_cast<const uint4*>(res + 8 * i8);
-            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              v[8 * i8 + 2 * j] += bf16lo(rw[j]);
-              v[8 * i8 + 2 * j + 1] += bf16hi(rw[j]);
-            }
+      } else {
+#pragma unroll 1
+        for (int r = 0; r < 2; ++r) {
+          uint32_t acc[64];
+          __syncwarp();
+          tmem_ld32(tbase + r * 64, acc);
+          tmem_ld32(tbase + r * 64 + 32, acc + 32);
+          tmem_ld_wait();
+          if (r == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(leader_empty);
           }
-        }
-        if (!p.d_f32) {
-          uint16_t* dst = static_cast<uint16_t*>(p.d) + row * p.ldd + col0;
-#pragma unroll
-          for (int i8 = 0; i8 < 4; ++i8) {
-            if (col0 + 8 * i8 >= p.n) break;
-            uint4 o;
-            o.x = pack_bf16x2(v[8 * i8 + 0], v[8 * i8 + 1]);
-            o.y = pack_bf16x2(v[8 * i8 + 2], v[8 * i8 + 3]);
-            o.z = pack_bf16x2(v[8 * i8 + 4], v[8 * i8 + 5]);
-            o.w = pack_bf16x2(v[8 * i8 + 6], v[8 * i8 + 7]);
-            reinterpret_cast<uint4*>(dst)[i8] = o;
-          }
-        } else {
-          float* dst = static_cast<float*>(p.d) + row * p.ldd + col0;
-#pragma unroll
-          for (int i4 = 0; i4 < 8; ++i4) {
-            if (col0 + 4 * i4 >= p.n) break;
-            float4 o = make_float4(v[4 * i4], v[4 * i4 + 1], v[4 * i4 + 2], v[4 * i4 + 3]);
-            if (p.accumulate) {
-              const float4 old = reinterpret_cast<const float4*>(dst)[i4];
-              o.x += old.x;
-              o.y += old.y;
-              o.z += old.z;
-              o.w += old.w;
-            }
-            reinterpret_cast<float4*>(dst)[i4] = o;
-          }
+          finish64(acc, p, alpha, row, colbase + r * 64, row_ok);
+          if (row_ok) store_f32_64(acc, p, row, colbase + r * 64);
         }
       }
     }
@@ -460,10 +598,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    tmem_dealloc2(tmem_base, TMEM_COLS);
   }
 }
 
@@ -488,35 +627,66 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D byte tensor [rows, row_bytes], box 128 bytes x box_rows, 128B swizzle.
-static bool make_operand_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box_rows) {
+// 2-D byte tensor [rows, row_bytes] with box {box_x bytes, box_rows}.
+static bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box_x, int box_rows,
+                     CUtensorMapSwizzle swz) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-  cuuint32_t box[2] = {(cuuint32_t)BK_BYTES, (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)box_x, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static int num_sms() {
-  static int cache[64] = {0};
+struct DeviceInfo {
+  int sms = 0;
+  int max_clusters = 0;
+};
+
+static DeviceInfo device_info() {
+  static std::mutex mu;
+  static DeviceInfo cache[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev);
-  return cache[dev] > 0 ? cache[dev] : 148;
+  if (dev < 0 || dev >= 64) return DeviceInfo{148, 74};
+  std::lock_guard<std::mutex> lk(mu);
+  DeviceInfo& d = cache[dev];
+  if (d.sms == 0) {
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * std::max(1, d.sms / 2), 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) ==
+            cudaSuccess &&
+        cudaOccupancyMaxActiveClusters(&n, nvfp4_gemm_kernel, &cfg) == cudaSuccess && n > 0)
+      d.max_clusters = n;
+    else
+      d.max_clusters = std::max(1, d.sms / 2);
+    cudaGetLastError();
+  }
+  return d;
 }
 
 static int run(const void* a, const void* b, const void* sfa, const void* sfb, const float* scale_a,
-               const float* scale_b, const void* bias, const void* residual, void* d, int d_dtype, int accumulate, int epilogue, int64_t m,
-               int64_t n, int64_t k, int64_t ldd, cudaStream_t stream) {
+               const float* scale_b, const void* bias, const void* residual, void* d, int d_dtype, int accumulate,
+               int epilogue, int64_t m, int64_t n, int64_t k, int64_t ldd, cudaStream_t stream) {
   if (!a || !b || !sfa || !sfb || !d) return NVFP4B200_ERR_INVALID_ARG;
   if (d_dtype != NVFP4B200_BF16 && d_dtype != NVFP4B200_F32) return NVFP4B200_ERR_INVALID_ARG;
   if (epilogue < 0 || epilogue > 2) return NVFP4B200_ERR_INVALID_ARG;
   if (accumulate && d_dtype != NVFP4B200_F32) return NVFP4B200_ERR_INVALID_ARG;
+  if (residual && d_dtype != NVFP4B200_BF16) return NVFP4B200_ERR_INVALID_ARG;
   if (m < 0 || n < 0 || k <= 0 || k % 32 || n % 8 || ldd < n || ldd % 8) return NVFP4B200_ERR_BAD_SHAPE;
   if (m > (1ll << 30) || n > (1ll << 30) || k > (1ll << 30)) return NVFP4B200_ERR_BAD_SHAPE;
   if (!aligned(a, 16) || !aligned(b, 16) || !aligned(sfa, 16) || !aligned(sfb, 16) || !aligned(d, 16) ||
@@ -526,11 +696,16 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   if (rc) return rc;
   if (m == 0 || n == 0) return NVFP4B200_OK;
 
-  CUtensorMap ma, mb;
-  if (!make_operand_map(&ma, a, m, k / 2, BM) || !make_operand_map(&mb, b, n, k / 2, BN)) return NVFP4B200_ERR_CUDA;
+  const int64_t sf_atoms = ceil_div(k, 64);
+  const int64_t pad_m = round_up(m, 128), pad_n = round_up(n, 128);
+  CUtensorMap ma, mb, msa, msb;
+  // scale tensors viewed as rows of 256 bytes (pad_rows * pad_cols is a multiple of 512)
+  if (!make_map(&ma, a, m, k / 2, BK_BYTES, CTA_M, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mb, b, n, k / 2, BK_BYTES, CTA_N, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&msa, sfa, pad_m * sf_atoms * 4 / 256, 256, 256, 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map(&msb, sfb, pad_n * sf_atoms * 4 / 256, 256, 256, 8, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return NVFP4B200_ERR_CUDA;
   Params p;
-  p.sfa = static_cast<const uint8_t*>(sfa);
-  p.sfb = static_cast<const uint8_t*>(sfb);
   p.scale_a = scale_a;
   p.scale_b = scale_b;
   p.bias = static_cast<const uint16_t*>(bias);
@@ -540,20 +715,20 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   p.n = n;
   p.k = k;
   p.ldd = ldd;
-  p.sf_atoms = ceil_div(k, 64);
-  p.sfb_groups = ceil_div(n, 128);
-  p.num_m_tiles = (int)ceil_div(m, BM);
-  p.num_n_tiles = (int)ceil_div(n, BN);
+  p.sf_atoms = sf_atoms;
+  p.num_m_tiles = (int)ceil_div(m, TILE_M);
+  p.num_n_tiles = (int)ceil_div(n, TILE_N);
   p.num_k_tiles = (int)ceil_div(k, BK);
   p.d_f32 = d_dtype == NVFP4B200_F32;
   p.accumulate = accumulate;
   p.epilogue = epilogue;
   const int64_t tiles = (int64_t)p.num_m_tiles * p.num_n_tiles;
-  const int grid = (int)std::min<int64_t>(tiles, num_sms());
+  const DeviceInfo info = device_info();
+  const int clusters = (int)std::min<int64_t>(tiles, info.max_clusters);
   if (cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
       cudaSuccess)
     return NVFP4B200_ERR_CUDA;
-  nvfp4_gemm_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+  nvfp4_gemm_kernel<<<2 * clusters, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, msa, msb, p);
   return launch_status();
 }
 
@@ -584,21 +759,21 @@ int nvfp4b200_gemm(const void* a, const void* b, const void* sfa, const void* sf
 
 int nvfp4b200_nvfp4_mm(const void* a, const void* b, const void* sfa, const void* sfb, const float* output_scale,
                        const void* bias, void* d, int64_t m, int64_t n, int64_t k, void* stream) {
-  return gemm::run(a, b, sfa, sfb, output_scale, nullptr, bias, nullptr, d, NVFP4B200_BF16, 0, NVFP4B200_EPI_NONE, m, n, k,
-                   n, (cudaStream_t)stream);
+  return gemm::run(a, b, sfa, sfb, output_scale, nullptr, bias, nullptr, d, NVFP4B200_BF16, 0, NVFP4B200_EPI_NONE, m,
+                   n, k, n, (cudaStream_t)stream);
 }
 
 int nvfp4b200_nvfp4_mm_relu(const void* a, const void* b, const void* sfa, const void* sfb, const float* output_scale,
                             const void* bias, void* d, int64_t m, int64_t n, int64_t k, void* stream) {
-  return gemm::run(a, b, sfa, sfb, output_scale, nullptr, bias, nullptr, d, NVFP4B200_BF16, 0, NVFP4B200_EPI_RELU, m, n, k,
-                   n, (cudaStream_t)stream);
+  return gemm::run(a, b, sfa, sfb, output_scale, nullptr, bias, nullptr, d, NVFP4B200_BF16, 0, NVFP4B200_EPI_RELU, m,
+                   n, k, n, (cudaStream_t)stream);
 }
 
 int nvfp4b200_nvfp4_mm_relu_2(const void* a, const void* b, const void* sfa, const void* sfb,
                               const float* output_scale, const void* bias, void* d, int64_t m, int64_t n, int64_t k,
                               void* stream) {
-  return gemm::run(a, b, sfa, sfb, output_scale, nullptr, bias, nullptr, d, NVFP4B200_BF16, 0, NVFP4B200_EPI_RELU2, m, n, k,
-                   n, (cudaStream_t)stream);
+  return gemm::run(a, b, sfa, sfb, output_scale, nullptr, bias, nullptr, d, NVFP4B200_BF16, 0, NVFP4B200_EPI_RELU2,
+                   m, n, k, n, (cudaStream_t)stream);
 }
 
 }  // extern "C"
