@@ -107,6 +107,20 @@ int nvfp4b200_quant_nvfp4_t(const void* x, const float* row_scale, const void* g
 int nvfp4b200_global_scale(const void* x, int64_t n, uint32_t* ws, float* global_scale_out,
                            float* amax_out, void* stream);
 
+/* Same result as nvfp4b200_global_scale, for callers that cannot allocate
+ * device memory (an arena or pool that owns all device memory, a plugin host
+ * that hands over only the call's tensors, or code that must not call
+ * cudaMalloc/cudaFree because those may synchronise the device).  No
+ * counterpart in the reference.  Allocates nothing: its scratch is a fixed
+ * ~16 KB array inside the library's device memory, held by every GPU that
+ * loads the library until the process exits.  Limit: n <= 2^30 elements
+ * (larger n returns NVFP4B200_ERR_BAD_SHAPE).  The first call on a device
+ * looks up the array's device address (make that first call before any
+ * stream capture).  All calls share the array: calls that overlap on the
+ * GPU race. */
+int nvfp4b200_global_scale_noalloc(const void* x, int64_t n, float* global_scale_out, float* amax_out,
+                                   void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Block-scaled GEMM (tcgen05.mma kind::mxf4nvf4)                           */
 /* ------------------------------------------------------------------------ */

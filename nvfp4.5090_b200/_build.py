@@ -18,7 +18,7 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 BUILD_DIR = os.path.join(PKG_DIR, "_build")
 LIB_DIR = os.path.join(PKG_DIR, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libnvfp4b200.so")
-SOURCES = ["quant.cu", "gemm.cu", "train.cu"]
+SOURCES = ["quant.cu", "gemm.cu", "train.cu", "noalloc.cu"]
 HEADERS = [os.path.join(CSRC, "common.cuh"), os.path.join(REPO_DIR, "include", "nvfp4_b200.h")]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"] + ARCH

@@ -31,6 +31,7 @@ SIGNATURES = {
     "nvfp4b200_rmsnorm_stats": [c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_void_p, c_void_p, c_void_p],
     "nvfp4b200_quant_nvfp4_t": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_void_p, c_void_p],
     "nvfp4b200_global_scale": [c_void_p, c_i64, c_void_p, c_void_p, c_void_p, c_void_p],
+    "nvfp4b200_global_scale_noalloc": [c_void_p, c_i64, c_void_p, c_void_p, c_void_p],
     "nvfp4b200_nvfp4_mm": [c_void_p] * 7 + [c_i64] * 3 + [c_void_p],
     "nvfp4b200_nvfp4_mm_relu": [c_void_p] * 7 + [c_i64] * 3 + [c_void_p],
     "nvfp4b200_nvfp4_mm_relu_2": [c_void_p] * 7 + [c_i64] * 3 + [c_void_p],
