@@ -48,14 +48,22 @@ __device__ int g_device_error = 0;
 
 namespace gemm {
 
-constexpr int TILE_M = 256, TILE_N = 256, BK = 256;  // pair tile; BK counts fp4 elements
+#ifndef NVFP4B200_SF_COPIER
+#define NVFP4B200_SF_COPIER 0  // 1: a separate warp copies scales to TMEM; 0: the MMA issuer does
+#endif
+#ifndef NVFP4B200_KBLOCKS_PER_STAGE
+#define NVFP4B200_KBLOCKS_PER_STAGE 4
+#endif
+constexpr int KBS = NVFP4B200_KBLOCKS_PER_STAGE;     // 64-k MMA blocks per pipeline stage (2 or 4)
+constexpr int TILE_M = 256, TILE_N = 256, BK = 64 * KBS;  // pair tile; BK counts fp4 elements
 constexpr int CTA_M = 128, CTA_N = 128;               // rows of A / B held by one CTA
-constexpr int BK_BYTES = BK / 2;                      // 128 bytes: one SW128 row
-constexpr int STAGES = 5;
-constexpr int A_BYTES = CTA_M * BK_BYTES;             // 16 KB
-constexpr int B_BYTES = CTA_N * BK_BYTES;             // 16 KB
-constexpr int SFA_BYTES = 2048;                       // 128 rows x 16 scales = 4 atoms
-constexpr int SFB_BYTES = 4096;                       // 2 row groups x 4 atoms
+constexpr int BK_BYTES = BK / 2;                      // one swizzle row: 64 B (SW64) or 128 B (SW128)
+constexpr int STAGES = KBS == 2 ? 10 : 5;             // same shared-memory bytes in flight either way
+constexpr int A_BYTES = CTA_M * BK_BYTES;
+constexpr int B_BYTES = CTA_N * BK_BYTES;
+constexpr int SFA_BYTES = 512 * KBS;                  // 128 rows x (KBS*4) scales = KBS atoms
+constexpr int SFB_BYTES = 1024 * KBS;                 // 2 row groups x KBS atoms
+constexpr int SFB_G1 = 512 * KBS;                     // offset of B's second row group
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
 constexpr uint32_t STAGE_TX = 2u * STAGE_BYTES;       // bytes landing per stage across the pair
 constexpr int EPI_WARPS = 8;
@@ -66,10 +74,13 @@ constexpr int ACC_COL = 0;
 // Scale columns: a ring with one slot per pipeline stage (A: 4 MMAs x 4
 // columns, B: 4 MMAs x 8 columns), so copies run ahead of the MMAs.
 constexpr int SF_COL0 = 256;
-constexpr int SF_SLOT_COLS = 48;
+constexpr int SF_SLOT_COLS = 12 * KBS;                // A: 4 columns, B: 8 columns per k-block
 static_assert(SF_COL0 + STAGES * SF_SLOT_COLS <= TMEM_COLS, "TMEM columns");
-constexpr int NUM_BARS = 3 * STAGES + 3;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int NUM_BARS = 3 * STAGES + 4;
+constexpr int BAR_BYTES = 512;                        // mbarriers + TMEM address slot + abort flag
+static_assert(NUM_BARS * 8 + 8 <= BAR_BYTES, "barrier area");
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;   // + worst-case 1 KB alignment
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;  // about 2 s at 2 GHz
 constexpr int GROUP_M = 8;                            // raster: 8 pair-rows (2048 rows) per group
 
@@ -114,8 +125,9 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
+// Arrive on a barrier of either CTA of the pair (address from mapa).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -154,6 +166,24 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
     }
   }
+}
+// Warp-wide bounded wait: every lane polls, the result is uniform across the warp.
+template <bool CLUSTER = false>
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  const bool ok = mbar_wait<CLUSTER>(bar, parity, abort_flag);
+  return __all_sync(0xffffffffu, ok);
+}
+// One lane of a converged warp (the lowest), chosen by elect.sync.  Async
+// tcgen05 / TMA instructions are issued under this predicate from warp-
+// uniform operands, so they issue from uniform registers.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}\n"
+      : "=r"(pred));
+  return pred != 0;
 }
 __device__ __forceinline__ void raise_abort(volatile int* abort_flag) {
   *abort_flag = 1;
@@ -230,6 +260,13 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
   return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
+// K-major with 64-byte swizzle: 8-row core groups 512 bytes apart, layout type 4.
+__device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (32ull << 32) | (1ull << 46) | (4ull << 61);
+}
+__device__ __forceinline__ uint64_t desc_operand(uint32_t saddr) {
+  return BK_BYTES == 128 ? desc_sw128(saddr) : desc_sw64(saddr);
+}
 // Descriptor of one 512-byte scale atom for tcgen05.cp 32x128b: 32 rows of
 // 16 bytes, no swizzle, 8-row core groups 128 bytes apart.
 __device__ __forceinline__ uint64_t desc_scales(uint32_t saddr) {
@@ -248,7 +285,7 @@ __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, 
 
 __device__ __forceinline__ int kblocks_in_tile(const Params& p, int kt) {
   const int64_t rem = p.k - (int64_t)kt * BK;
-  return (int)imin64(4, (rem + 63) / 64);
+  return (int)imin64(KBS, (rem + 63) / 64);
 }
 
 __device__ __forceinline__ float apply_epi(float v, int epi) {
@@ -351,7 +388,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   auto sf_ready_bar = [&](int s) { return smem_u32(bars + 2 * STAGES + s); };  // leader: scales in TMEM
   const uint32_t tmem_full_bar = smem_u32(bars + 3 * STAGES);
   const uint32_t tmem_empty_bar = smem_u32(bars + 3 * STAGES + 1);
-  const uint32_t drain_bar = smem_u32(bars + 3 * STAGES + 2);
+  const uint32_t drain_bar = smem_u32(bars + 3 * STAGES + 2);     // MMA issuer's error-path drain
+  const uint32_t cp_drain_bar = smem_u32(bars + 3 * STAGES + 3);  // copier's error-path drain
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -362,6 +400,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     mbar_init(tmem_full_bar, 1);
     mbar_init(tmem_empty_bar, 2 * EPI_WARPS);
     mbar_init(drain_bar, 1);
+    mbar_init(cp_drain_bar, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tmap(&tmap_a);
@@ -384,97 +423,113 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const int num_clusters = gridDim.x >> 1;
 
   if (warp == 0) {
-    // ---------------- TMA producer (both CTAs) ----------------
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int armed_phase[STAGES];
-      for (int s = 0; s < STAGES; ++s) armed_phase[s] = -1;
-      bool ok = true;
-      for (int tile = cluster_id; ok && tile < total_tiles; tile += num_clusters) {
-        int mb, nb;
-        tile_coords(tile, p, mb, nb);
-        const int a_row = mb * TILE_M + (int)rank * CTA_M;
-        const int b_row = nb * TILE_N + (int)rank * CTA_N;
-        const int sfa_group = 2 * mb + (int)rank;
-        for (int kt = 0; kt < p.num_k_tiles; ++kt) {
-          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          const uint32_t lbar = map_to_rank(full_bar(stage), 0);
-          if (leader) {
-            mbar_expect_tx(full_bar(stage), STAGE_TX);
-            armed_phase[stage] = (int)phase;
-          }
+    // ---------------- TMA producer (both CTAs, whole warp; one lane issues) ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t armed = 0, armed_parity = 0;  // leader: stages whose barrier expects bytes, and the phase armed
+    bool ok = true;
+    for (int tile = cluster_id; ok && tile < total_tiles; tile += num_clusters) {
+      int mb, nb;
+      tile_coords(tile, p, mb, nb);
+      const int a_row = mb * TILE_M + (int)rank * CTA_M;
+      const int b_row = nb * TILE_N + (int)rank * CTA_N;
+      // scale slabs are rows of 256 bytes; slab (group, kt) starts at row (group * atoms + KBS * kt) * 2
+      const int64_t sfa_row0 = ((int64_t)(2 * mb + (int)rank) * p.sf_atoms) * 2;
+      const int64_t sfb_row0 = ((int64_t)(2 * nb) * p.sf_atoms) * 2;
+      const int64_t sfb_row1 = ((int64_t)(2 * nb + 1) * p.sf_atoms) * 2;
+      for (int kt = 0; kt < p.num_k_tiles; ++kt) {
+        if (!warp_wait(empty_bar(stage), phase ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t lbar = map_to_rank(full_bar(stage), 0);
+        const int sf_dy = 2 * KBS * kt;
+        if (elect_one()) {
+          if (leader) mbar_expect_tx(full_bar(stage), STAGE_TX);
           tma_load_2d_pair(smem_u32(sA + stage * A_BYTES), &tmap_a, lbar, kt * BK_BYTES, a_row);
           tma_load_2d_pair(smem_u32(sB + stage * B_BYTES), &tmap_b, lbar, kt * BK_BYTES, b_row);
-          // scale slabs: rows of 256 bytes; slab (group, kt) starts at row (group*atoms + 4*kt)*2
-          tma_load_2d_pair(smem_u32(sSFA + stage * SFA_BYTES), &tmap_sfa, lbar, 0,
-                           (int)(((int64_t)sfa_group * p.sf_atoms + 4 * kt) * 2));
-          tma_load_2d_pair(smem_u32(sSFB + stage * SFB_BYTES), &tmap_sfb, lbar, 0,
-                           (int)(((int64_t)(2 * nb) * p.sf_atoms + 4 * kt) * 2));
-          tma_load_2d_pair(smem_u32(sSFB + stage * SFB_BYTES + 2048), &tmap_sfb, lbar, 0,
-                           (int)(((int64_t)(2 * nb + 1) * p.sf_atoms + 4 * kt) * 2));
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
+          tma_load_2d_pair(smem_u32(sSFA + stage * SFA_BYTES), &tmap_sfa, lbar, 0, (int)(sfa_row0 + sf_dy));
+          tma_load_2d_pair(smem_u32(sSFB + stage * SFB_BYTES), &tmap_sfb, lbar, 0, (int)(sfb_row0 + sf_dy));
+          tma_load_2d_pair(smem_u32(sSFB + stage * SFB_BYTES + SFB_G1), &tmap_sfb, lbar, 0, (int)(sfb_row1 + sf_dy));
+        }
+        __syncwarp();
+        armed |= 1u << stage;
+        armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
         }
       }
-      if (!ok) {
-        raise_abort(abort_flag);
-        if (leader) {  // the leader's stage barriers count both CTAs' copies
-          const long long t0 = clock64();
-          for (int s = 0; s < STAGES; ++s) {
-            if (armed_phase[s] < 0) continue;
-            while (!mbar_try_wait(full_bar(s), (uint32_t)armed_phase[s]) && clock64() - t0 < WAIT_LIMIT_CYCLES) {
-            }
+    }
+    if (!ok && lane == 0) {
+      raise_abort(abort_flag);
+      if (leader) {  // the leader's stage barriers count both CTAs' copies: let them land
+        const long long t0 = clock64();
+        for (int st = 0; st < STAGES; ++st) {
+          if (!((armed >> st) & 1u)) continue;
+          while (!mbar_try_wait(full_bar(st), (armed_parity >> st) & 1u) && clock64() - t0 < WAIT_LIMIT_CYCLES) {
           }
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer (leader CTA) ----------------
-    if (leader && lane == 0) {
+    // ---------------- MMA issuer (leader CTA, whole warp; one lane issues) ----------------
+    if (leader) {
       int stage = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true, issued = false;
       const uint32_t acc = tmem_base + ACC_COL;
       for (int tile = cluster_id; ok && tile < total_tiles; tile += num_clusters) {
-        if (!mbar_wait<true>(tmem_empty_bar, acc_phase ^ 1, abort_flag)) {
+        if (!warp_wait<true>(tmem_empty_bar, acc_phase ^ 1, abort_flag)) {
           ok = false;
           break;
         }
         acc_phase ^= 1;
         tc_fence_after();
         for (int kt = 0; kt < p.num_k_tiles; ++kt) {
+#if NVFP4B200_SF_COPIER
           // scales of this stage are in TMEM (which implies its operands landed)
-          if (!mbar_wait(sf_ready_bar(stage), phase, abort_flag)) {
+          if (!warp_wait(sf_ready_bar(stage), phase, abort_flag)) {
+#else
+          if (!warp_wait<true>(full_bar(stage), phase, abort_flag)) {
+#endif
             ok = false;
             break;
           }
           tc_fence_after();
           const int nkb = kblocks_in_tile(p, kt);
           const uint32_t sfa_t = tmem_base + SF_COL0 + SF_SLOT_COLS * stage;
-          const uint32_t sfb_t = sfa_t + 16;
-          const uint64_t adesc = desc_sw128(smem_u32(sA + stage * A_BYTES));
-          const uint64_t bdesc = desc_sw128(smem_u32(sB + stage * B_BYTES));
-          for (int j = 0; j < nkb; ++j) {
-            // advance 32 bytes (64 fp4) along K inside the swizzled 128-byte row
-            tc_mma_pair(acc, adesc + 2 * j, bdesc + 2 * j, sfa_t + 4 * j, sfb_t + 8 * j, (kt | j) != 0);
+          const uint32_t sfb_t = sfa_t + 4 * KBS;
+          const uint64_t adesc = desc_operand(smem_u32(sA + stage * A_BYTES));
+          const uint64_t bdesc = desc_operand(smem_u32(sB + stage * B_BYTES));
+#if !NVFP4B200_SF_COPIER
+          const uint64_t sfa_d = desc_scales(smem_u32(sSFA + stage * SFA_BYTES));
+          const uint64_t sfb_d = desc_scales(smem_u32(sSFB + stage * SFB_BYTES));
+#endif
+          if (elect_one()) {
+            for (int j = 0; j < nkb; ++j) {
+#if !NVFP4B200_SF_COPIER
+              tc_cp_scales_pair(sfa_t + 4 * j, sfa_d + 32 * j);  // +512 bytes per atom
+              tc_cp_scales_pair(sfb_t + 8 * j, sfb_d + 32 * j);
+              tc_cp_scales_pair(sfb_t + 8 * j + 4, sfb_d + (SFB_G1 >> 4) + 32 * j);
+#endif
+              // advance 32 bytes (64 fp4) along K inside the swizzled row
+              tc_mma_pair(acc, adesc + 2 * j, bdesc + 2 * j, sfa_t + 4 * j, sfb_t + 8 * j, (kt | j) != 0);
+            }
+            tc_commit_pair(empty_bar(stage));
           }
+          __syncwarp();
           issued = true;
-          tc_commit_pair(empty_bar(stage));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        tc_commit_pair(tmem_full_bar);
+        if (elect_one()) tc_commit_pair(tmem_full_bar);
+        __syncwarp();
       }
-      if (!ok) {
+      if (!ok && elect_one()) {  // the lane that issued the MMAs commits the drain
         raise_abort(abort_flag);
         if (issued) {
           tc_commit_pair(drain_bar);
@@ -484,9 +539,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+#if NVFP4B200_SF_COPIER
   } else if (warp == COPIER_WARP) {
-    // ---------------- scale copier (leader CTA) ----------------
-    if (leader && lane == 0) {
+    // ---------------- scale copier (leader CTA, whole warp; one lane issues) ----------------
+    if (leader) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true, issued = false;
@@ -494,39 +550,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         for (int kt = 0; kt < p.num_k_tiles; ++kt) {
           // operands and scale atoms of both CTAs landed; the slot's previous MMAs are
           // done (the producer refilled the stage only after they released it)
-          if (!mbar_wait<true>(full_bar(stage), phase, abort_flag)) {
+          if (!warp_wait<true>(full_bar(stage), phase, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const int nkb = kblocks_in_tile(p, kt);
-          const uint32_t sfa_s = smem_u32(sSFA + stage * SFA_BYTES);
-          const uint32_t sfb_s = smem_u32(sSFB + stage * SFB_BYTES);
+          const uint64_t sfa_d = desc_scales(smem_u32(sSFA + stage * SFA_BYTES));
+          const uint64_t sfb_d = desc_scales(smem_u32(sSFB + stage * SFB_BYTES));
           const uint32_t sfa_t = tmem_base + SF_COL0 + SF_SLOT_COLS * stage;
-          const uint32_t sfb_t = sfa_t + 16;
-          for (int j = 0; j < nkb; ++j) {
-            tc_cp_scales_pair(sfa_t + 4 * j, desc_scales(sfa_s + 512 * j));
-            tc_cp_scales_pair(sfb_t + 8 * j, desc_scales(sfb_s + 512 * j));
-            tc_cp_scales_pair(sfb_t + 8 * j + 4, desc_scales(sfb_s + 2048 + 512 * j));
+          const uint32_t sfb_t = sfa_t + 4 * KBS;
+          if (elect_one()) {
+            for (int j = 0; j < nkb; ++j) {
+              tc_cp_scales_pair(sfa_t + 4 * j, sfa_d + 32 * j);  // +512 bytes per atom
+              tc_cp_scales_pair(sfb_t + 8 * j, sfb_d + 32 * j);
+              tc_cp_scales_pair(sfb_t + 8 * j + 4, sfb_d + (SFB_G1 >> 4) + 32 * j);
+            }
+            tc_commit_local(sf_ready_bar(stage));
           }
+          __syncwarp();
           issued = true;
-          tc_commit_local(sf_ready_bar(stage));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      if (!ok) {
+      if (!ok && elect_one()) {
         raise_abort(abort_flag);
         if (issued) {
-          tc_commit_local(drain_bar);
+          tc_commit_local(cp_drain_bar);
           const long long t0 = clock64();
-          while (!mbar_try_wait(drain_bar, 0) && clock64() - t0 < WAIT_LIMIT_CYCLES) {
+          while (!mbar_try_wait(cp_drain_bar, 0) && clock64() - t0 < WAIT_LIMIT_CYCLES) {
           }
         }
       }
     }
+#else
+  } else if (warp == COPIER_WARP) {
+    // no copier warp: the MMA issuer copies the scales itself
+#endif
   } else {
     // ---------------- epilogue (warps 2..9, both CTAs) ----------------
     const int quad = warp & 3;               // TMEM lanes [32*quad, 32*quad+32)
@@ -700,10 +763,11 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   const int64_t pad_m = round_up(m, 128), pad_n = round_up(n, 128);
   CUtensorMap ma, mb, msa, msb;
   // scale tensors viewed as rows of 256 bytes (pad_rows * pad_cols is a multiple of 512)
-  if (!make_map(&ma, a, m, k / 2, BK_BYTES, CTA_M, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mb, b, n, k / 2, BK_BYTES, CTA_N, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&msa, sfa, pad_m * sf_atoms * 4 / 256, 256, 256, 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map(&msb, sfb, pad_n * sf_atoms * 4 / 256, 256, 256, 8, CU_TENSOR_MAP_SWIZZLE_NONE))
+  const CUtensorMapSwizzle swz = BK_BYTES == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  if (!make_map(&ma, a, m, k / 2, BK_BYTES, CTA_M, swz) ||
+      !make_map(&mb, b, n, k / 2, BK_BYTES, CTA_N, swz) ||
+      !make_map(&msa, sfa, pad_m * sf_atoms * 4 / 256, 256, 256, 2 * KBS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map(&msb, sfb, pad_n * sf_atoms * 4 / 256, 256, 256, 2 * KBS, CU_TENSOR_MAP_SWIZZLE_NONE))
     return NVFP4B200_ERR_CUDA;
   Params p;
   p.scale_a = scale_a;
