@@ -19,19 +19,23 @@
 //               tcgen05 scale-atom layout: a 128-row x 256-k slab is 2 KB
 //               contiguous, loaded as a 2-D box over 256-byte rows).  All
 //               loads signal the leader CTA's stage barrier.
-//   warp 10     scale copier (leader CTA): tcgen05.cp.cta_group::2 moves each
-//               scale atom into both CTAs' TMEM (32x128b.warpx4: 4 columns x
-//               128 lanes) into a per-stage ring slot and commits to a
-//               "scales ready" barrier.  Issued from its own thread, the copies
-//               for later stages overlap the MMAs of earlier ones (a single
-//               issuing thread's copies and MMAs execute strictly in order).
 //   warp 1      TMEM allocator (both CTAs) and, in the leader CTA, the MMA
-//               issuer: 4 MMAs 256x256x64 per 256-k stage; tcgen05.commit
-//               multicasts stage release / accumulator-ready to both CTAs.
+//               issuer: per 256-k stage, 12 tcgen05.cp.cta_group::2 scale
+//               copies (32x128b.warpx4: one 512-byte atom -> 4 columns x 128
+//               lanes in both CTAs) and 4 MMAs 256x256x64.  One thread's
+//               tcgen05 operations execute in issue order, so one scale slot
+//               is reused by every stage.  tcgen05.commit multicasts stage
+//               release / accumulator-ready to both CTAs.
 //   warps 2-9   epilogue (both CTAs): two warps per TMEM lane quadrant, each
-//               drains 128 columns in two 64-column rounds, releases the
-//               accumulator to the leader's MMA warp, then stores, so the
-//               stores overlap the next tile's main loop.
+//               drains 128 columns in two 64-column chunks and stores them.
+// TMEM holds two 256-column accumulators that share 64 columns (buffer 0:
+// [0,256), buffer 1: [192,448)) plus the scale slot [448,496).  Tiles
+// alternate buffers; the epilogue drains the shared 64 columns first and
+// releases them, so the next tile's MMAs start while the epilogue is still
+// draining and storing the rest.
+// The producer, MMA and epilogue loops run on converged warps; TMA, copy and
+// MMA instructions are issued by one elect.sync-chosen lane from warp-uniform
+// operands.
 // Every mbarrier wait is bounded: on timeout the CTA records
 // NVFP4B200_ERR_TIMEOUT in a device error word, drains what it issued and
 // returns, so a broken pipeline cannot hang the GPU.  No TMA load uses
@@ -40,6 +44,7 @@
 
 #include <cuda.h>
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 namespace nvfp4b200 {
@@ -48,38 +53,32 @@ __device__ int g_device_error = 0;
 
 namespace gemm {
 
-#ifndef NVFP4B200_SF_COPIER
-#define NVFP4B200_SF_COPIER 0  // 1: a separate warp copies scales to TMEM; 0: the MMA issuer does
-#endif
-#ifndef NVFP4B200_KBLOCKS_PER_STAGE
-#define NVFP4B200_KBLOCKS_PER_STAGE 4
-#endif
-constexpr int KBS = NVFP4B200_KBLOCKS_PER_STAGE;     // 64-k MMA blocks per pipeline stage (2 or 4)
-constexpr int TILE_M = 256, TILE_N = 256, BK = 64 * KBS;  // pair tile; BK counts fp4 elements
+constexpr int TILE_M = 256, TILE_N = 256, BK = 256;   // pair tile; BK counts fp4 elements per stage
+constexpr int KBLOCKS = BK / 64;                      // MMAs (K = 64) per stage
 constexpr int CTA_M = 128, CTA_N = 128;               // rows of A / B held by one CTA
-constexpr int BK_BYTES = BK / 2;                      // one swizzle row: 64 B (SW64) or 128 B (SW128)
-constexpr int STAGES = KBS == 2 ? 10 : 5;             // same shared-memory bytes in flight either way
+constexpr int BK_BYTES = BK / 2;                      // one 128-byte swizzle row per operand row
+constexpr int STAGES = 5;
 constexpr int A_BYTES = CTA_M * BK_BYTES;
 constexpr int B_BYTES = CTA_N * BK_BYTES;
-constexpr int SFA_BYTES = 512 * KBS;                  // 128 rows x (KBS*4) scales = KBS atoms
-constexpr int SFB_BYTES = 1024 * KBS;                 // 2 row groups x KBS atoms
-constexpr int SFB_G1 = 512 * KBS;                     // offset of B's second row group
+constexpr int SFA_BYTES = 512 * KBLOCKS;              // 128 rows x 16 scales = 4 atoms
+constexpr int SFB_BYTES = 1024 * KBLOCKS;             // 2 row groups x 4 atoms
+constexpr int SFB_G1 = 512 * KBLOCKS;                 // offset of B's second row group
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
 constexpr uint32_t STAGE_TX = 2u * STAGE_BYTES;       // bytes landing per stage across the pair
 constexpr int EPI_WARPS = 8;
-constexpr int COPIER_WARP = 2 + EPI_WARPS;
-constexpr int NUM_THREADS = 32 * (COPIER_WARP + 1);
+constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS);
 constexpr int TMEM_COLS = 512;
-constexpr int ACC_COL = 0;
-// Scale columns: a ring with one slot per pipeline stage (A: 4 MMAs x 4
-// columns, B: 4 MMAs x 8 columns), so copies run ahead of the MMAs.
-constexpr int SF_COL0 = 256;
-constexpr int SF_SLOT_COLS = 12 * KBS;                // A: 4 columns, B: 8 columns per k-block
-static_assert(SF_COL0 + STAGES * SF_SLOT_COLS <= TMEM_COLS, "TMEM columns");
-constexpr int NUM_BARS = 3 * STAGES + 4;
+constexpr int ACC_COLS = 256;                         // one accumulator buffer
+constexpr int ACC1_COL = 192;                         // buffer 1 starts inside buffer 0's last 64 columns
+constexpr int SF_COL = 448;                           // scale slot: A 4 x 4 columns, then B 4 x 8 columns
+constexpr int SF_COLS = 12 * KBLOCKS;
+static_assert(ACC1_COL + ACC_COLS <= SF_COL && SF_COL + SF_COLS <= TMEM_COLS, "TMEM columns");
+constexpr int NUM_BARS = 2 * STAGES + 3;           // full, empty, tmem_full, overlap_free, drain
 constexpr int BAR_BYTES = 512;                        // mbarriers + TMEM address slot + abort flag
 static_assert(NUM_BARS * 8 + 8 <= BAR_BYTES, "barrier area");
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;   // + worst-case 1 KB alignment
+constexpr int OUT_CHUNK_BYTES = 32 * 128;             // one epilogue warp's 32 rows x 64 bf16 output chunk
+constexpr int OUT_BYTES = EPI_WARPS * OUT_CHUNK_BYTES;  // bf16 output staging for the TMA stores
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024 + BAR_BYTES;  // + worst-case 1 KB alignment
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;  // about 2 s at 2 GHz
 constexpr int GROUP_M = 8;                            // raster: 8 pair-rows (2048 rows) per group
@@ -199,6 +198,23 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       "l"(map), "r"(bar), "r"(x), "r"(y)
       : "memory");
 }
+// 2-D tiled TMA store of a shared-memory box (bulk async-group of the issuing thread).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// This thread's bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// This thread's bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
@@ -223,10 +239,6 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
       "h"(mask)
       : "memory");
-}
-// Arrive once on `bar` in this CTA when this thread's prior tcgen05 pair operations complete.
-__device__ __forceinline__ void tc_commit_local(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ void tc_cp_scales_pair(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
@@ -260,13 +272,6 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
   return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
-// K-major with 64-byte swizzle: 8-row core groups 512 bytes apart, layout type 4.
-__device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr) {
-  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (32ull << 32) | (1ull << 46) | (4ull << 61);
-}
-__device__ __forceinline__ uint64_t desc_operand(uint32_t saddr) {
-  return BK_BYTES == 128 ? desc_sw128(saddr) : desc_sw64(saddr);
-}
 // Descriptor of one 512-byte scale atom for tcgen05.cp 32x128b: 32 rows of
 // 16 bytes, no swizzle, 8-row core groups 128 bytes apart.
 __device__ __forceinline__ uint64_t desc_scales(uint32_t saddr) {
@@ -285,7 +290,7 @@ __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, 
 
 __device__ __forceinline__ int kblocks_in_tile(const Params& p, int kt) {
   const int64_t rem = p.k - (int64_t)kt * BK;
-  return (int)imin64(KBS, (rem + 63) / 64);
+  return (int)imin64(KBLOCKS, (rem + 63) / 64);
 }
 
 __device__ __forceinline__ float apply_epi(float v, int epi) {
@@ -369,6 +374,7 @@ __device__ __forceinline__ void store_f32_64(const uint32_t* v, const Params& p,
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
+                      const __grid_constant__ CUtensorMap tmap_d,
                       const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -376,7 +382,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   uint8_t* sB = sA + STAGES * A_BYTES;
   uint8_t* sSFA = sB + STAGES * B_BYTES;
   uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sSFB + STAGES * SFB_BYTES);
+  uint8_t* sOut = sSFB + STAGES * SFB_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + OUT_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -385,28 +392,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const bool leader = rank == 0;
   auto full_bar = [&](int s) { return smem_u32(bars + s); };             // leader: all bytes of the stage landed
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };    // both: MMAs done with the stage
-  auto sf_ready_bar = [&](int s) { return smem_u32(bars + 2 * STAGES + s); };  // leader: scales in TMEM
-  const uint32_t tmem_full_bar = smem_u32(bars + 3 * STAGES);
-  const uint32_t tmem_empty_bar = smem_u32(bars + 3 * STAGES + 1);
-  const uint32_t drain_bar = smem_u32(bars + 3 * STAGES + 2);     // MMA issuer's error-path drain
-  const uint32_t cp_drain_bar = smem_u32(bars + 3 * STAGES + 3);  // copier's error-path drain
+  const uint32_t tmem_full_bar = smem_u32(bars + 2 * STAGES);            // both: a tile's accumulator is final
+  const uint32_t overlap_free_bar = smem_u32(bars + 2 * STAGES + 1);     // leader: shared columns drained
+  const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 2);            // leader: error-path drain
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
-      mbar_init(sf_ready_bar(s), 1);
     }
     mbar_init(tmem_full_bar, 1);
-    mbar_init(tmem_empty_bar, 2 * EPI_WARPS);
+    mbar_init(overlap_free_bar, 2 * EPI_WARPS);
     mbar_init(drain_bar, 1);
-    mbar_init(cp_drain_bar, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
     prefetch_tmap(&tmap_sfa);
     prefetch_tmap(&tmap_sfb);
+    if (!p.d_f32) prefetch_tmap(&tmap_d);
   }
   if (warp == 1) {
     tmem_alloc2(smem_u32(tmem_slot), TMEM_COLS);
@@ -433,7 +437,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       tile_coords(tile, p, mb, nb);
       const int a_row = mb * TILE_M + (int)rank * CTA_M;
       const int b_row = nb * TILE_N + (int)rank * CTA_N;
-      // scale slabs are rows of 256 bytes; slab (group, kt) starts at row (group * atoms + KBS * kt) * 2
+      // scale slabs are rows of 256 bytes; slab (group, kt) starts at row (group * atoms + 4 * kt) * 2
       const int64_t sfa_row0 = ((int64_t)(2 * mb + (int)rank) * p.sf_atoms) * 2;
       const int64_t sfb_row0 = ((int64_t)(2 * nb) * p.sf_atoms) * 2;
       const int64_t sfb_row1 = ((int64_t)(2 * nb + 1) * p.sf_atoms) * 2;
@@ -443,7 +447,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         const uint32_t lbar = map_to_rank(full_bar(stage), 0);
-        const int sf_dy = 2 * KBS * kt;
+        const int sf_dy = 2 * KBLOCKS * kt;
         if (elect_one()) {
           if (leader) mbar_expect_tx(full_bar(stage), STAGE_TX);
           tma_load_2d_pair(smem_u32(sA + stage * A_BYTES), &tmap_a, lbar, kt * BK_BYTES, a_row);
@@ -476,43 +480,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     // ---------------- MMA issuer (leader CTA, whole warp; one lane issues) ----------------
     if (leader) {
       int stage = 0;
-      uint32_t phase = 0, acc_phase = 0;
+      uint32_t phase = 0;
       bool ok = true, issued = false;
-      const uint32_t acc = tmem_base + ACC_COL;
-      for (int tile = cluster_id; ok && tile < total_tiles; tile += num_clusters) {
-        if (!warp_wait<true>(tmem_empty_bar, acc_phase ^ 1, abort_flag)) {
+      const uint32_t sfa_t = tmem_base + SF_COL;
+      const uint32_t sfb_t = sfa_t + 4 * KBLOCKS;
+      int it = 0;  // tiles of this cluster so far; buffer = it & 1
+      for (int tile = cluster_id; ok && tile < total_tiles; tile += num_clusters, ++it) {
+        // The previous tile's epilogue has drained the 64 columns its buffer
+        // shares with this tile's buffer.  Every epilogue warp finished the tile
+        // before it first, so this buffer's own previous use is drained too.
+        if (!warp_wait<true>(overlap_free_bar, (it & 1) ^ 1, abort_flag)) {
           ok = false;
           break;
         }
-        acc_phase ^= 1;
         tc_fence_after();
+        const uint32_t acc = tmem_base + ((it & 1) ? ACC1_COL : 0);
         for (int kt = 0; kt < p.num_k_tiles; ++kt) {
-#if NVFP4B200_SF_COPIER
-          // scales of this stage are in TMEM (which implies its operands landed)
-          if (!warp_wait(sf_ready_bar(stage), phase, abort_flag)) {
-#else
+          // operands and scale atoms of both CTAs landed
           if (!warp_wait<true>(full_bar(stage), phase, abort_flag)) {
-#endif
             ok = false;
             break;
           }
           tc_fence_after();
           const int nkb = kblocks_in_tile(p, kt);
-          const uint32_t sfa_t = tmem_base + SF_COL0 + SF_SLOT_COLS * stage;
-          const uint32_t sfb_t = sfa_t + 4 * KBS;
-          const uint64_t adesc = desc_operand(smem_u32(sA + stage * A_BYTES));
-          const uint64_t bdesc = desc_operand(smem_u32(sB + stage * B_BYTES));
-#if !NVFP4B200_SF_COPIER
+          const uint64_t adesc = desc_sw128(smem_u32(sA + stage * A_BYTES));
+          const uint64_t bdesc = desc_sw128(smem_u32(sB + stage * B_BYTES));
           const uint64_t sfa_d = desc_scales(smem_u32(sSFA + stage * SFA_BYTES));
           const uint64_t sfb_d = desc_scales(smem_u32(sSFB + stage * SFB_BYTES));
-#endif
           if (elect_one()) {
             for (int j = 0; j < nkb; ++j) {
-#if !NVFP4B200_SF_COPIER
               tc_cp_scales_pair(sfa_t + 4 * j, sfa_d + 32 * j);  // +512 bytes per atom
               tc_cp_scales_pair(sfb_t + 8 * j, sfb_d + 32 * j);
               tc_cp_scales_pair(sfb_t + 8 * j + 4, sfb_d + (SFB_G1 >> 4) + 32 * j);
-#endif
               // advance 32 bytes (64 fp4) along K inside the swizzled row
               tc_mma_pair(acc, adesc + 2 * j, bdesc + 2 * j, sfa_t + 4 * j, sfb_t + 8 * j, (kt | j) != 0);
             }
@@ -539,124 +538,91 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
-#if NVFP4B200_SF_COPIER
-  } else if (warp == COPIER_WARP) {
-    // ---------------- scale copier (leader CTA, whole warp; one lane issues) ----------------
-    if (leader) {
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true, issued = false;
-      for (int tile = cluster_id; ok && tile < total_tiles; tile += num_clusters) {
-        for (int kt = 0; kt < p.num_k_tiles; ++kt) {
-          // operands and scale atoms of both CTAs landed; the slot's previous MMAs are
-          // done (the producer refilled the stage only after they released it)
-          if (!warp_wait<true>(full_bar(stage), phase, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const int nkb = kblocks_in_tile(p, kt);
-          const uint64_t sfa_d = desc_scales(smem_u32(sSFA + stage * SFA_BYTES));
-          const uint64_t sfb_d = desc_scales(smem_u32(sSFB + stage * SFB_BYTES));
-          const uint32_t sfa_t = tmem_base + SF_COL0 + SF_SLOT_COLS * stage;
-          const uint32_t sfb_t = sfa_t + 4 * KBS;
-          if (elect_one()) {
-            for (int j = 0; j < nkb; ++j) {
-              tc_cp_scales_pair(sfa_t + 4 * j, sfa_d + 32 * j);  // +512 bytes per atom
-              tc_cp_scales_pair(sfb_t + 8 * j, sfb_d + 32 * j);
-              tc_cp_scales_pair(sfb_t + 8 * j + 4, sfb_d + (SFB_G1 >> 4) + 32 * j);
-            }
-            tc_commit_local(sf_ready_bar(stage));
-          }
-          __syncwarp();
-          issued = true;
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-      }
-      if (!ok && elect_one()) {
-        raise_abort(abort_flag);
-        if (issued) {
-          tc_commit_local(cp_drain_bar);
-          const long long t0 = clock64();
-          while (!mbar_try_wait(cp_drain_bar, 0) && clock64() - t0 < WAIT_LIMIT_CYCLES) {
-          }
-        }
-      }
-    }
-#else
-  } else if (warp == COPIER_WARP) {
-    // no copier warp: the MMA issuer copies the scales itself
-#endif
   } else {
     // ---------------- epilogue (warps 2..9, both CTAs) ----------------
     const int quad = warp & 3;               // TMEM lanes [32*quad, 32*quad+32)
     const int half = (warp - 2) >> 2;        // accumulator columns [128*half, 128*half+128)
-    const uint32_t leader_empty = map_to_rank(tmem_empty_bar, 0);
+    const uint32_t leader_overlap_free = map_to_rank(overlap_free_bar, 0);
     const float alpha = (p.scale_a ? *p.scale_a : 1.0f) * (p.scale_b ? *p.scale_b : 1.0f);
-    uint32_t acc_phase = 0;
-    for (int tile = cluster_id; tile < total_tiles; tile += num_clusters) {
+    int it = 0;
+    for (int tile = cluster_id; tile < total_tiles; tile += num_clusters, ++it) {
       int mb, nb;
       tile_coords(tile, p, mb, nb);
-      bool ok = mbar_wait(tmem_full_bar, acc_phase, abort_flag);
+      bool ok = mbar_wait(tmem_full_bar, (uint32_t)(it & 1), abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
         if (lane == 0) raise_abort(abort_flag);
         break;
       }
-      acc_phase ^= 1;
       tc_fence_after();
+      const int buf = it & 1;
+      // This warp's 64-column chunk inside the columns the two buffers share is
+      // drained first: buffer 0's tile columns [192,256) (half 1, chunk 1) and
+      // buffer 1's tile columns [0,64) (half 0, chunk 0).
+      const int first = (buf == 0 && half == 1) ? 1 : 0;
       const int64_t row = (int64_t)mb * TILE_M + (int64_t)rank * CTA_M + quad * 32 + lane;
       const bool row_ok = row < p.m;
       const int64_t colbase = (int64_t)nb * TILE_N + half * 128;
-      const uint32_t tbase = tmem_base + ACC_COL + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * 128);
+      const uint32_t tbase =
+          tmem_base + (buf ? ACC1_COL : 0) + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * 128);
       if (!p.d_f32) {
-        uint16_t* dst = static_cast<uint16_t*>(p.d) + row * p.ldd + colbase;
+        // bf16: each 32-row x 64-column chunk goes through this warp's shared
+        // staging buffer (128-byte swizzle: 16-byte piece j of row i at
+        // (j ^ (i % 8)) * 16) and out with one TMA store, which drops rows and
+        // columns outside the matrix.
+        const uint32_t obuf = smem_u32(sOut + (warp - 2) * OUT_CHUNK_BYTES);
+        const uint32_t orow = obuf + lane * 128;
+        const int y0 = mb * TILE_M + (int)rank * CTA_M + quad * 32;
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
+          const int c = r ^ first;
           uint32_t acc[64];
           __syncwarp();
-          tmem_ld32(tbase + r * 64, acc);
-          tmem_ld32(tbase + r * 64 + 32, acc + 32);
+          tmem_ld32(tbase + c * 64, acc);
+          tmem_ld32(tbase + c * 64 + 32, acc + 32);
           tmem_ld_wait();
-          if (r == 1) {  // every accumulator column of this warp is in registers: release TMEM
+          if (r == 0) {  // the shared columns are in registers: the next tile's MMAs may start
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(leader_empty);
+            if (lane == 0) mbar_arrive_cluster(leader_overlap_free);
           }
-          finish64(acc, p, alpha, row, colbase + r * 64, row_ok);
-          if (row_ok) {
+          finish64(acc, p, alpha, row, colbase + c * 64, row_ok);
+          if (lane == 0) bulk_wait_read();  // the previous store has read the staging buffer
+          __syncwarp();
 #pragma unroll
-            for (int i8 = 0; i8 < 8; ++i8) {
-              if (colbase + r * 64 + 8 * i8 < p.n)
-                reinterpret_cast<uint4*>(dst + r * 64)[i8] = make_uint4(
-                    pack_bf16x2(__uint_as_float(acc[8 * i8 + 0]), __uint_as_float(acc[8 * i8 + 1])),
-                    pack_bf16x2(__uint_as_float(acc[8 * i8 + 2]), __uint_as_float(acc[8 * i8 + 3])),
-                    pack_bf16x2(__uint_as_float(acc[8 * i8 + 4]), __uint_as_float(acc[8 * i8 + 5])),
-                    pack_bf16x2(__uint_as_float(acc[8 * i8 + 6]), __uint_as_float(acc[8 * i8 + 7])));
-            }
+          for (int j = 0; j < 8; ++j)
+            st_shared_v4(orow + ((j ^ (lane & 7)) << 4),
+                         pack_bf16x2(__uint_as_float(acc[8 * j + 0]), __uint_as_float(acc[8 * j + 1])),
+                         pack_bf16x2(__uint_as_float(acc[8 * j + 2]), __uint_as_float(acc[8 * j + 3])),
+                         pack_bf16x2(__uint_as_float(acc[8 * j + 4]), __uint_as_float(acc[8 * j + 5])),
+                         pack_bf16x2(__uint_as_float(acc[8 * j + 6]), __uint_as_float(acc[8 * j + 7])));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && y0 < p.m && colbase + c * 64 < p.n) {  // x in bytes (the map views d as bytes)
+            tma_store_2d(&tmap_d, obuf, (int)(2 * (colbase + c * 64)), y0);
+            bulk_commit();
           }
         }
       } else {
 #pragma unroll 1
         for (int r = 0; r < 2; ++r) {
+          const int c = r ^ first;
           uint32_t acc[64];
           __syncwarp();
-          tmem_ld32(tbase + r * 64, acc);
-          tmem_ld32(tbase + r * 64 + 32, acc + 32);
+          tmem_ld32(tbase + c * 64, acc);
+          tmem_ld32(tbase + c * 64 + 32, acc + 32);
           tmem_ld_wait();
-          if (r == 1) {
+          if (r == 0) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(leader_empty);
+            if (lane == 0) mbar_arrive_cluster(leader_overlap_free);
           }
-          finish64(acc, p, alpha, row, colbase + r * 64, row_ok);
-          if (row_ok) store_f32_64(acc, p, row, colbase + r * 64);
+          finish64(acc, p, alpha, row, colbase + c * 64, row_ok);
+          if (row_ok) store_f32_64(acc, p, row, colbase + c * 64);
         }
       }
     }
+    if (lane == 0) bulk_wait_all();  // output stores complete before the CTA exits
   }
 
   tc_fence_before();
@@ -692,11 +658,11 @@ static EncodeTiledFn encode_fn() {
 
 // 2-D byte tensor [rows, row_bytes] with box {box_x bytes, box_rows}.
 static bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box_x, int box_rows,
-                     CUtensorMapSwizzle swz) {
+                     CUtensorMapSwizzle swz, int64_t stride_bytes = 0) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint64_t strides[1] = {(cuuint64_t)(stride_bytes ? stride_bytes : row_bytes)};
   cuuint32_t box[2] = {(cuuint32_t)box_x, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
@@ -761,13 +727,17 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
 
   const int64_t sf_atoms = ceil_div(k, 64);
   const int64_t pad_m = round_up(m, 128), pad_n = round_up(n, 128);
-  CUtensorMap ma, mb, msa, msb;
+  CUtensorMap ma, mb, msa, msb, md;
+  memset(&md, 0, sizeof(md));
   // scale tensors viewed as rows of 256 bytes (pad_rows * pad_cols is a multiple of 512)
-  const CUtensorMapSwizzle swz = BK_BYTES == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B;
   if (!make_map(&ma, a, m, k / 2, BK_BYTES, CTA_M, swz) ||
       !make_map(&mb, b, n, k / 2, BK_BYTES, CTA_N, swz) ||
-      !make_map(&msa, sfa, pad_m * sf_atoms * 4 / 256, 256, 256, 2 * KBS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map(&msb, sfb, pad_n * sf_atoms * 4 / 256, 256, 256, 2 * KBS, CU_TENSOR_MAP_SWIZZLE_NONE))
+      !make_map(&msa, sfa, pad_m * sf_atoms * 4 / 256, 256, 256, 2 * KBLOCKS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map(&msb, sfb, pad_n * sf_atoms * 4 / 256, 256, 256, 2 * KBLOCKS, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return NVFP4B200_ERR_CUDA;
+  // bf16 output viewed as bytes: [m rows, 2n bytes], row stride 2*ldd, boxes of 32 rows x 128 bytes
+  if (d_dtype == NVFP4B200_BF16 && !make_map(&md, d, m, 2 * n, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B, 2 * ldd))
     return NVFP4B200_ERR_CUDA;
   Params p;
   p.scale_a = scale_a;
@@ -792,7 +762,7 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   if (cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
       cudaSuccess)
     return NVFP4B200_ERR_CUDA;
-  nvfp4_gemm_kernel<<<2 * clusters, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, msa, msb, p);
+  nvfp4_gemm_kernel<<<2 * clusters, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, msa, msb, md, p);
   return launch_status();
 }
 
