@@ -56,34 +56,46 @@ __device__ __forceinline__ float e4m3_decode(uint32_t c) {
                 : __uint_as_float(((e + 120u) << 23) | (m << 20));
 }
 
-// 3-bit E2M1 magnitude code of ax = |f * inv_scale| given its float bits b.
+// Pack 8 floats into 8 E2M1 nibbles (low nibble = even element,
+// float4utils.py:141), each nibble equal to the reference's comparison ladder
+// (float4utils.py:127-139): magnitude code = #{t in {0.25,0.75,1.25,1.75,
+// 2.5,3.5,5} : !(|f * inv_scale| < t)} after clamping to 6 (ties round away
+// from zero, NaN gives 7), sign bit = (f < 0).
 //
-// Equivalent to the reference's comparison ladder (float4utils.py:127-137):
-// code = #{t in {0.25,0.75,1.25,1.75,2.5,3.5,5} : !(ax < t)} after clamping
-// ax to 6 -- ties round away from zero and NaN gives 7.  For ax >= 1 the
-// E2M1 grid is a 1-bit mantissa, so adding half a bit-22 unit and keeping
-// exponent + top mantissa bit rounds half-up; the result is capped at the
-// code of 6.0.  Below 1 the grid is {0, 0.5, 1}: two threshold compares.
-// Positive IEEE floats (and +inf/NaN with the sign cleared) order like
-// unsigned integers, so every comparison is an integer comparison.
-__device__ __forceinline__ uint32_t e2m1_code_from_bits(uint32_t b) {
-  const uint32_t hi = min((b + 0x00200000u) >> 22, 259u) - 252u;
-  const uint32_t lo = (uint32_t)(b >= 0x3E800000u) + (uint32_t)(b >= 0x3F400000u);
-  return b >= 0x3F800000u ? hi : lo;
+// The conversion instruction cvt.rn.satfinite.e2m1x2.f32 rounds to nearest
+// with ties to even and saturates to +-6.  Three adjustments of its input
+// make it equal to the ladder for every f32 input:
+//   * p = fma(f, inv_scale, +0): the product rounded once, except that
+//     f = -0.0 gives +0 (the reference's sign test f < 0 is false there),
+//     while a negative product that underflows keeps its sign;
+//   * bits | 1: every tie point of the E2M1 grid has a zero lowest mantissa
+//     bit, so setting it moves an exact tie just above the tie (rounding away
+//     from zero) and cannot move any other value across a tie;
+//   * min(bits, 0xFF7FFFFF): -inf (whose "| 1" would be a NaN) becomes
+//     -FLT_MAX, which saturates to -6 like the ladder; arithmetic NaN results
+//     are the positive canonical NaN, which the instruction turns into +6.
+// An exhaustive GPU sweep over every f32 bit pattern checks this identity.
+__device__ __forceinline__ float fma_plus_zero(float a, float b) {
+  float r;
+  asm("fma.rn.f32 %0, %1, %2, 0f00000000;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
-
-// 4-bit nibble of one element: sign bit from ``f < 0`` on the unscaled value
-// (float4utils.py:133-139), magnitude from the ladder above.
-__device__ __forceinline__ uint32_t e2m1_nibble(float f, float inv_scale) {
-  const float ax = fabsf(f * inv_scale);
-  return e2m1_code_from_bits(__float_as_uint(ax)) | (f < 0.0f ? 8u : 0u);
+__device__ __forceinline__ float e2m1_input(float f, float inv_scale) {
+  return __uint_as_float(min(__float_as_uint(fma_plus_zero(f, inv_scale)), 0xFF7FFFFFu) | 1u);
 }
-
-// Pack 8 floats into 8 nibbles (low nibble = even element, float4utils.py:141).
 __device__ __forceinline__ uint32_t encode8(const float (&f)[8], float inv_scale) {
-  uint32_t out = 0;
+  float q[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) out |= e2m1_nibble(f[i], inv_scale) << (4 * i);
+  for (int i = 0; i < 8; ++i) q[i] = e2m1_input(f[i], inv_scale);
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(out)
+      : "f"(q[0]), "f"(q[1]), "f"(q[2]), "f"(q[3]), "f"(q[4]), "f"(q[5]), "f"(q[6]), "f"(q[7]));
   return out;
 }
 

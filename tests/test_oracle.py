@@ -59,23 +59,55 @@ def test_e2m1_ladder_ties_away_from_zero():
     assert list(orc.e2m1_encode(special, np.float32(1.0))) == [0, 0, 7, 7, 15, 7, 8]
 
 
-def _e2m1_code_from_bits(b: np.ndarray) -> np.ndarray:
-    """numpy restatement of the kernel's integer E2M1 encoder (common.cuh)."""
-    b = b.astype(np.uint64)
-    hi = np.minimum((b + 0x00200000) >> 22, 259) - 252
-    lo = (b >= 0x3E800000).astype(np.uint64) + (b >= 0x3F400000).astype(np.uint64)
-    return np.where(b >= 0x3F800000, hi, lo).astype(np.uint8)
+_E2M1_GRID = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
 
 
-def test_integer_e2m1_encoder_equals_ladder():
-    hi16 = np.arange(0, 0x8000, dtype=np.uint32) << 16
-    lows = np.array([0, 1, 0x7FFF, 0x8000, 0xFFFF], dtype=np.uint32)
+def _e2m1_rne_satfinite(x: np.ndarray) -> np.ndarray:
+    """numpy model of cvt.rn.satfinite.e2m1x2.f32 on one value: nearest grid
+    point, ties to the even code, saturation to +-6, sign kept, NaN -> +6
+    (the behaviour the kernel's encoder relies on; a GPU sweep checks it)."""
+    x = x.astype(np.float64)
+    ax = np.abs(x)
+    d = np.abs(ax[:, None] - _E2M1_GRID[None, :])
+    best = d.min(axis=1, keepdims=True)
+    cand = d == best
+    two = cand.sum(axis=1) > 1
+    code = np.where(two, np.argmax(cand & (np.arange(8) % 2 == 0)[None, :], axis=1), np.argmax(cand, axis=1))
+    code = np.where(ax >= 6.0, 7, code)
+    code = np.where(np.signbit(x), code | 8, code)
+    return np.where(np.isnan(x), 7, code).astype(np.uint8)
+
+
+def _kernel_e2m1_input(p: np.ndarray) -> np.ndarray:
+    """numpy restatement of common.cuh e2m1_input after the fma: min(bits, 0xFF7FFFFF) | 1."""
+    b = p.astype(np.float32).view(np.uint32)
+    return (np.minimum(b, np.uint32(0xFF7FFFFF)) | np.uint32(1)).view(np.float32)
+
+
+def test_hardware_e2m1_encoder_identity_equals_ladder():
+    """Round-to-nearest-even E2M1 of (bits | 1), with -inf clamped, equals the
+    reference's ties-away ladder for every f32 except -0.0, which the kernel's
+    fma(f, inv_scale, +0) turns into +0 first."""
+    hi16 = np.arange(0, 0x10000, dtype=np.uint32) << 16
+    lows = np.array([0, 1, 2, 0x7FFF, 0x8000, 0xFFFF], dtype=np.uint32)
     bits = (hi16[:, None] | lows[None, :]).reshape(-1)
+    thr = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0], np.float32).view(np.uint32)
+    near = (thr[:, None].astype(np.int64) + np.arange(-3, 4)[None, :]).reshape(-1).astype(np.uint32)
     rng = np.random.default_rng(0)
-    bits = np.concatenate([bits, rng.integers(0, 0x7FFFFFFF, 1 << 20, dtype=np.uint32)])
-    ax = bits.view(np.float32)
-    ref = orc.e2m1_encode(ax, np.float32(1.0)) & 7
-    assert np.array_equal(_e2m1_code_from_bits(bits), ref)
+    bits = np.concatenate([bits, near, near | 0x80000000, rng.integers(0, 0xFFFFFFFF, 1 << 18, dtype=np.uint32)])
+    bits = bits[bits != 0x80000000]
+    p = bits.view(np.float32)
+    # the fma's NaN results are the positive canonical NaN 0x7FFFFFFF
+    p_fma = np.where(np.isnan(p), np.uint32(0x7FFFFFFF).view(np.float32), p)
+    with np.errstate(invalid="ignore", over="ignore"):
+        got = _e2m1_rne_satfinite(_kernel_e2m1_input(p_fma))
+    ref = orc.e2m1_encode(p, np.float32(1.0))
+    bad = np.nonzero(got != ref)[0]
+    assert bad.size == 0, [(hex(int(bits[i])), int(got[i]), int(ref[i])) for i in bad[:8]]
+    # the fma with +0 maps -0.0 to +0 but keeps the sign of a negative underflow
+    assert np.signbit(np.float32(-0.0) * np.float32(3.0))          # plain product keeps -0 ...
+    assert not np.signbit(np.float32(-0.0) * np.float32(3.0) + np.float32(0.0))  # ... + 0 clears it
+
 
 
 def test_swizzle_matches_reference_formula_and_is_bijective():
