@@ -80,13 +80,18 @@ __device__ __forceinline__ float fma_plus_zero(float a, float b) {
   asm("fma.rn.f32 %0, %1, %2, 0f00000000;" : "=f"(r) : "f"(a), "f"(b));
   return r;
 }
+// CLAMP = false skips the -inf adjustment; valid whenever the block amax is
+// finite (then no product is -inf).
+template <bool CLAMP = true>
 __device__ __forceinline__ float e2m1_input(float f, float inv_scale) {
-  return __uint_as_float(min(__float_as_uint(fma_plus_zero(f, inv_scale)), 0xFF7FFFFFu) | 1u);
+  const uint32_t b = __float_as_uint(fma_plus_zero(f, inv_scale));
+  return __uint_as_float((CLAMP ? min(b, 0xFF7FFFFFu) : b) | 1u);
 }
-__device__ __forceinline__ uint32_t encode8(const float (&f)[8], float inv_scale) {
+template <bool CLAMP = true>
+__device__ __forceinline__ uint32_t encode8(const float* f, float inv_scale) {
   float q[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) q[i] = e2m1_input(f[i], inv_scale);
+  for (int i = 0; i < 8; ++i) q[i] = e2m1_input<CLAMP>(f[i], inv_scale);
   uint32_t out;
   asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
       "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
@@ -113,6 +118,47 @@ __device__ __forceinline__ uint32_t block_scale(float amax, float g, float inv_g
     inv_scale = (s > 0.0f) ? __frcp_rn(s * g) : 1.0f;
   }
   return code;
+}
+
+// 16 floats (one block) -> 8 bytes of nibbles, the -inf adjustment only when
+// the block amax is infinite.
+__device__ __forceinline__ uint2 encode16(const float (&f)[16], float inv_scale, float amax) {
+  if (amax <= 3.402823466e38f) return make_uint2(encode8<false>(f, inv_scale), encode8<false>(f + 8, inv_scale));
+  return make_uint2(encode8<true>(f, inv_scale), encode8<true>(f + 8, inv_scale));
+}
+
+// E4M3 block-scale code of a block amax (float4utils.py:109-116 with the
+// global scale folded in): e4m3_satfinite((amax * (1/6)) * inv_g), 0 when
+// amax == 0.  The matching 1/(scale * g) comes from inv_scale_table.
+__device__ __forceinline__ uint32_t block_code(float amax, float inv_g) {
+  return amax > 0.0f ? e4m3_rn_satfinite((amax * (1.0f / 6.0f)) * inv_g) : 0u;
+}
+
+// Table of inv_scale for every block-scale code under global scale g:
+// 1 / (decode(c) * g) rounded once (the value block_scale computes), 1 for a
+// zero scale.  Filled by the CTA's threads before first use.
+__device__ __forceinline__ void fill_inv_scale_table(float* tab, float g) {
+  for (int c = threadIdx.x; c < 256; c += blockDim.x) {
+    const float sv = e4m3_decode((uint32_t)c & 0x7Fu);
+    tab[c] = sv > 0.0f ? __frcp_rn(sv * g) : 1.0f;
+  }
+}
+
+// Block amax of 16 bf16 values held as 8 words: integer max of |x| bit
+// patterns.  Returns the 16-bit pattern (above 0x7F80 means a NaN is present).
+__device__ __forceinline__ uint32_t absmax16_bits(const uint32_t (&w)[8]) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = __vmaxu2(m, w[i] & 0x7FFF7FFFu);
+  return max(m & 0xFFFFu, m >> 16);
+}
+
+// fmaxf-semantics amax over 16 floats (NaN dropped).
+__device__ __forceinline__ float fmax_abs16(const float (&f)[16]) {
+  float a = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a = fmaxf(a, fabsf(f[i]));
+  return a;
 }
 
 // Block amax of 8 bf16 values held as 4 words: integer max of |x| bit

@@ -79,90 +79,161 @@ __global__ void __launch_bounds__(256) global_amax_kernel(const uint4* __restric
 }
 
 // ---------------------------------------------------------------------------
-// tile quantizer: 128 rows x 256 columns per CTA
+// tile quantizer: 128 rows x 512 columns per CTA
 // ---------------------------------------------------------------------------
+// Each lane owns one 16-element block column of the tile (32 B of every row);
+// a warp covers 16 rows, read 4 rows per pass with the next pass's loads in
+// flight while the current one is encoded.  Per row a warp reads 1 KB and
+// writes 256 B of nibbles; the tile's 8 scale atoms (4 KB, contiguous in the
+// swizzled layout) are staged in shared memory and written whole.
 
 constexpr int QT_ROWS = 128;
-constexpr int QT_COLS = 256;       // 16 blocks = 4 scale atoms
+constexpr int QT_COLS = 512;       // 32 blocks = 8 scale atoms
 constexpr int QT_THREADS = 256;    // 8 warps x 16 rows
+constexpr int QT_PASS = 4;         // rows per pipelined pass
+
+__device__ __forceinline__ void unpack16(const uint4 a, const uint4 b, uint32_t (&w)[8], float (&f)[16]) {
+  w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) { f[2 * i] = bf16lo(w[i]); f[2 * i + 1] = bf16hi(w[i]); }
+}
 
 template <bool HAS_ROW, bool HAS_GAMMA>
 __global__ void __launch_bounds__(QT_THREADS) quant_tile_kernel(
     const uint16_t* __restrict__ x, const float* __restrict__ row_scale,
     const uint16_t* __restrict__ gamma, uint8_t* __restrict__ q, uint8_t* __restrict__ s,
-    int64_t rows, int64_t k, int64_t pad_cols, const float* __restrict__ gptr) {
-  __shared__ __align__(16) uint8_t s_tile[4 * 512];
+    int64_t rows, int64_t k, int64_t pad_cols, const float* __restrict__ gptr, int q8) {
+  __shared__ __align__(16) uint8_t s_tile[8 * 512];
+  __shared__ float inv_tab[256];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int64_t r0 = (int64_t)blockIdx.y * QT_ROWS;
-  const int64_t c0 = (int64_t)blockIdx.x * QT_COLS;  // element column
-  const int64_t col = c0 + 8 * lane;
-  const bool col_ok = col < k;
+  const int64_t tile_r0 = (int64_t)blockIdx.y * QT_ROWS;
+  const int64_t col = (int64_t)blockIdx.x * QT_COLS + 16 * lane;  // this lane's block
+  const bool col_ok = col < k;                                    // k % 16 == 0: all or nothing
   const float g = load_global_scale(gptr);
   const float inv_g = __frcp_rn(g);
+  fill_inv_scale_table(inv_tab, g);
 
-  float gam[8];
+  float gam[16];
   if (HAS_GAMMA) {
-    uint4 gv = make_uint4(0, 0, 0, 0);
-    if (col_ok) gv = __ldg(reinterpret_cast<const uint4*>(gamma + col));
-    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) { gam[2 * i] = bf16lo(gw[i]); gam[2 * i + 1] = bf16hi(gw[i]); }
-  }
-
-  // issue all 16 row loads of this warp first (memory-level parallelism)
-  uint4 v[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int64_t r = r0 + wid * 16 + i;
-    v[i] = make_uint4(0, 0, 0, 0);
-    if (col_ok && r < rows) v[i] = __ldg(reinterpret_cast<const uint4*>(x + r * k + col));
-  }
-
-  const int blk = lane >> 1;             // block index inside the 256-col tile (0..15)
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int rl = wid * 16 + i;         // row inside the tile
-    const int64_t r = r0 + rl;
-    const bool ok = col_ok && r < rows;
-    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-    float f[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) { f[2 * j] = bf16lo(w[j]); f[2 * j + 1] = bf16hi(w[j]); }
-    float amax;
-    if (HAS_ROW || HAS_GAMMA) {
-      const float rs = HAS_ROW ? (ok ? __ldg(row_scale + r) : 0.0f) : 1.0f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (HAS_ROW) f[j] = f[j] * rs;
-        if (HAS_GAMMA) f[j] = f[j] * gam[j];
-      }
-      amax = fmax_abs8(f);
-    } else {
-      uint32_t mb = absmax8_bits(w);
-      amax = (mb > 0x7F80u) ? fmax_abs8(f) : __uint_as_float(mb << 16);
+    uint4 ga = make_uint4(0, 0, 0, 0), gb = ga;
+    if (col_ok) {
+      ga = __ldg(reinterpret_cast<const uint4*>(gamma + col));
+      gb = __ldg(reinterpret_cast<const uint4*>(gamma + col) + 1);
     }
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    float inv_scale;
-    const uint32_t code = ok ? block_scale(amax, g, inv_g, inv_scale) : 0u;
-    if (!ok) inv_scale = 1.0f;
-    const uint32_t packed = encode8(f, inv_scale);
-    if (ok) *reinterpret_cast<uint32_t*>(q + r * (k >> 1) + (col >> 1)) = packed;
-    if ((lane & 1) == 0) s_tile[(blk >> 2) * 512 + atom_offset(rl, blk & 3)] = (uint8_t)code;
+    uint32_t gw[8];
+    unpack16(ga, gb, gw, gam);
+  }
+  __syncthreads();  // inv_tab
+
+  auto load_pass = [&](int pass, uint4 (&buf)[QT_PASS][2]) {
+#pragma unroll
+    for (int i = 0; i < QT_PASS; ++i) {
+      const int64_t r = tile_r0 + wid * 16 + pass * QT_PASS + i;
+      buf[i][0] = make_uint4(0, 0, 0, 0);
+      buf[i][1] = buf[i][0];
+      if (col_ok && r < rows) {
+        const uint4* p = reinterpret_cast<const uint4*>(x + r * k + col);
+        buf[i][0] = __ldg(p);
+        buf[i][1] = __ldg(p + 1);
+      }
+    }
+  };
+  uint4 cur[QT_PASS][2], nxt[QT_PASS][2];
+  load_pass(0, cur);
+#pragma unroll
+  for (int pass = 0; pass < 16 / QT_PASS; ++pass) {
+    if (pass + 1 < 16 / QT_PASS) load_pass(pass + 1, nxt);
+#pragma unroll
+    for (int i = 0; i < QT_PASS; ++i) {
+      const int rl = wid * 16 + pass * QT_PASS + i;  // row inside the tile
+      const int64_t r = tile_r0 + rl;
+      const bool ok = col_ok && r < rows;
+      uint32_t w[8];
+      float f[16];
+      unpack16(cur[i][0], cur[i][1], w, f);
+      float amax;
+      if (HAS_ROW || HAS_GAMMA) {
+        const float rs = HAS_ROW ? (r < rows ? __ldg(row_scale + r) : 0.0f) : 1.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (HAS_ROW) f[j] = f[j] * rs;
+          if (HAS_GAMMA) f[j] = f[j] * gam[j];
+        }
+        amax = fmax_abs16(f);
+      } else {
+        const uint32_t mb = absmax16_bits(w);
+        amax = (mb > 0x7F80u) ? fmax_abs16(f) : __uint_as_float(mb << 16);
+      }
+      const uint32_t code = ok ? block_code(amax, inv_g) : 0u;
+      const uint2 packed = encode16(f, inv_tab[code], amax);
+      if (ok) {
+        uint8_t* dst = q + r * (k >> 1) + (col >> 1);
+        if (q8) {
+          *reinterpret_cast<uint2*>(dst) = packed;
+        } else {
+          reinterpret_cast<uint32_t*>(dst)[0] = packed.x;
+          reinterpret_cast<uint32_t*>(dst)[1] = packed.y;
+        }
+      }
+      s_tile[(lane >> 2) * 512 + atom_offset(rl, lane & 3)] = (uint8_t)code;
+    }
+    if (pass + 1 < 16 / QT_PASS) {
+#pragma unroll
+      for (int i = 0; i < QT_PASS; ++i) { cur[i][0] = nxt[i][0]; cur[i][1] = nxt[i][1]; }
+    }
   }
   __syncthreads();
-  // write the (up to) 4 atoms of this tile: contiguous 2 KB in the swizzled tensor
-  const int64_t atom0 = (int64_t)blockIdx.x * 4;
-  const int64_t n_atoms = imin64(4, (pad_cols >> 2) - atom0);
+  // the (up to) 8 atoms of this tile: contiguous 4 KB of the swizzled tensor
+  const int64_t atom0 = (int64_t)blockIdx.x * 8;
+  const int64_t n_atoms = imin64(8, (pad_cols >> 2) - atom0);
   const int64_t dst = ((int64_t)blockIdx.y * (pad_cols >> 2) + atom0) * 512;
-  if ((int64_t)threadIdx.x * 8 < n_atoms * 512)
-    *reinterpret_cast<uint2*>(s + dst + threadIdx.x * 8) = reinterpret_cast<const uint2*>(s_tile)[threadIdx.x];
+  if ((int64_t)threadIdx.x * 16 < n_atoms * 512)
+    *reinterpret_cast<uint4*>(s + dst + threadIdx.x * 16) = reinterpret_cast<const uint4*>(s_tile)[threadIdx.x];
 }
 
 // ---------------------------------------------------------------------------
 // fused RMSNorm -> quantize: one warp per row, the row held in registers
 // ---------------------------------------------------------------------------
+// Lane L of the warp owns the 16-element blocks c = 32 j + L (chunk j of 512
+// columns).  The sum of squares reproduces the reference's fp32 order exactly
+// (float4utils.py:183-222, 256 threads per row): thread t accumulates
+// ``sum_sq += a0 * a0 + a1 * a1`` over its blocks t, t + 256, ... word by
+// word; each warp of 32 threads reduces with shfl_down 16, 8, 4, 2, 1; the 8
+// warp sums are reduced the same way by warp 0.  Here virtual thread
+// t = 32 m + L is lane L's partial sum m = j mod 8, the 8 warp trees are run
+// on the 8 partials, and the last tree over 8 values (the other 24 lanes hold
+// 0) is written out in registers.
 
 constexpr int RMS_WARPS = 4;
+
+// Sum of squares of one 16-element block, accumulated into `acc` in the
+// reference's order.
+__device__ __forceinline__ float sumsq_block(float acc, const uint4 v0, const uint4 v1) {
+  const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float a0 = bf16lo(w[i]), a1 = bf16hi(w[i]);
+    acc += a0 * a0 + a1 * a1;
+  }
+  return acc;
+}
+
+// The reference's two-level shfl_down reduction of the 256 per-thread sums,
+// given lane L's partial sums for threads L, 32 + L, ..., 224 + L.  Result
+// valid in every lane.
+__device__ __forceinline__ float reduce_like_reference(float (&ps)[8]) {
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ps[m] += __shfl_down_sync(0xffffffffu, ps[m], off);
+  }
+  // warp 0's tree over (s0..s7, 0, ..., 0): offsets 16 and 8 add zeros
+  const float t0 = (ps[0] + 0.0f) + ps[4], t1 = (ps[1] + 0.0f) + ps[5];
+  const float t2 = (ps[2] + 0.0f) + ps[6], t3 = (ps[3] + 0.0f) + ps[7];
+  const float total = (t0 + t2) + (t1 + t3);
+  return __shfl_sync(0xffffffffu, total, 0);
+}
 
 // MODE 0: quantize (computes inv_rms, writes it).  MODE 1: statistics only
 // (inv_rms + global amax of the normalised row).
@@ -171,31 +242,37 @@ __global__ void __launch_bounds__(RMS_WARPS * 32) rmsnorm_row_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma, uint8_t* __restrict__ q,
     uint8_t* __restrict__ s, float* __restrict__ inv_rms_out, int64_t rows, int64_t pad_rows,
     int64_t k, int64_t pad_cols, float eps, const float* __restrict__ gptr, uint32_t* ws,
-    float* g_out) {
+    float* g_out, int q8) {
+  __shared__ float inv_tab[256];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int64_t r = (int64_t)blockIdx.x * RMS_WARPS + wid;
   const bool row_ok = r < rows;
-  uint4 v[NV];
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int64_t col = (int64_t)j * 256 + 8 * lane;
-    v[j] = make_uint4(0, 0, 0, 0);
-    if (row_ok && col < k) v[j] = __ldg(reinterpret_cast<const uint4*>(x + r * k + col));
+  const int64_t nblk = k >> 4;
+  float g = 1.0f, inv_g = 1.0f;
+  if (MODE == 0) {
+    g = load_global_scale(gptr);
+    inv_g = __frcp_rn(g);
+    fill_inv_scale_table(inv_tab, g);
+    __syncthreads();
   }
-  // sum of squares in fp32 (thread-sequential, then a butterfly)
-  float ss = 0.0f;
+  uint4 v[NV][2];
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float a0 = bf16lo(w[i]), a1 = bf16hi(w[i]);
-      ss += a0 * a0 + a1 * a1;
+    const int64_t c = 32 * j + lane;
+    v[j][0] = make_uint4(0, 0, 0, 0);
+    v[j][1] = v[j][0];
+    if (row_ok && c < nblk) {
+      const uint4* p = reinterpret_cast<const uint4*>(x + r * k + 16 * c);
+      v[j][0] = __ldg(p);
+      v[j][1] = __ldg(p + 1);
     }
   }
+  float ps[8];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float inv = rsqrtf(ss / (float)k + eps);
+  for (int m = 0; m < 8; ++m) ps[m] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) ps[j & 7] = sumsq_block(ps[j & 7], v[j][0], v[j][1]);
+  const float inv = rsqrtf((reduce_like_reference(ps) / (float)k) + eps);
   if (row_ok && lane == 0 && inv_rms_out) inv_rms_out[r] = inv;
 
   if (MODE == 1) {
@@ -203,21 +280,22 @@ __global__ void __launch_bounds__(RMS_WARPS * 32) rmsnorm_row_kernel(
     if (row_ok) {
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
-        const int64_t col = (int64_t)j * 256 + 8 * lane;
-        if (col >= k) continue;
-        const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-        float gam[8];
+        const int64_t c = 32 * j + lane;
+        if (c >= nblk) continue;
+        uint32_t w[8];
+        float f[16];
+        unpack16(v[j][0], v[j][1], w, f);
+        float gam[16];
         if (HAS_GAMMA) {
-          const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gamma + col));
-          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) { gam[2 * i] = bf16lo(gw[i]); gam[2 * i + 1] = bf16hi(gw[i]); }
+          const uint4* gp = reinterpret_cast<const uint4*>(gamma + 16 * c);
+          uint32_t gw[8];
+          unpack16(__ldg(gp), __ldg(gp + 1), gw, gam);
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float a0 = bf16lo(w[i]) * inv, a1 = bf16hi(w[i]) * inv;
-          if (HAS_GAMMA) { a0 = a0 * gam[2 * i]; a1 = a1 * gam[2 * i + 1]; }
-          am = fmaxf(am, fmaxf(fabsf(a0), fabsf(a1)));
+        for (int i = 0; i < 16; ++i) {
+          float a = f[i] * inv;
+          if (HAS_GAMMA) a = a * gam[i];
+          am = fmaxf(am, fabsf(a));
         }
       }
     }
@@ -225,61 +303,68 @@ __global__ void __launch_bounds__(RMS_WARPS * 32) rmsnorm_row_kernel(
     return;
   }
 
-  const float g = load_global_scale(gptr);
-  const float inv_g = __frcp_rn(g);
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    const int64_t col = (int64_t)j * 256 + 8 * lane;
-    if ((int64_t)j * 256 >= pad_cols * 16) break;  // whole chunk beyond the padded scale columns
-    const bool ok = row_ok && col < k;
-    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-    float f[8];
+    const int64_t c = 32 * j + lane;              // block column of this lane
+    if (32 * j >= pad_cols) continue;             // whole chunk beyond the padded scale columns
+    const bool ok = row_ok && c < nblk;
+    uint32_t w[8];
+    float f[16];
+    unpack16(v[j][0], v[j][1], w, f);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) { f[2 * i] = bf16lo(w[i]) * inv; f[2 * i + 1] = bf16hi(w[i]) * inv; }
+    for (int i = 0; i < 16; ++i) f[i] = f[i] * inv;
     if (HAS_GAMMA && ok) {
-      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gamma + col));
-      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+      const uint4* gp = reinterpret_cast<const uint4*>(gamma + 16 * c);
+      uint32_t gw[8];
+      float gam[16];
+      unpack16(__ldg(gp), __ldg(gp + 1), gw, gam);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) { f[2 * i] = f[2 * i] * bf16lo(gw[i]); f[2 * i + 1] = f[2 * i + 1] * bf16hi(gw[i]); }
+      for (int i = 0; i < 16; ++i) f[i] = f[i] * gam[i];
     }
-    float amax = fmax_abs8(f);
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    float inv_scale = 1.0f;
-    uint32_t code = ok ? block_scale(amax, g, inv_g, inv_scale) : 0u;
-    const uint32_t packed = encode8(f, inv_scale);
-    if (ok) *reinterpret_cast<uint32_t*>(q + r * (k >> 1) + (col >> 1)) = packed;
-    // gather the 4 block scales of each 4-block group into one word
-    const uint32_t c1 = __shfl_down_sync(0xffffffffu, code, 2);
-    const uint32_t c2 = __shfl_down_sync(0xffffffffu, code, 4);
-    const uint32_t c3 = __shfl_down_sync(0xffffffffu, code, 6);
-    const int64_t bcol = (int64_t)j * 16 + (lane >> 1);  // block column of this lane
-    if ((lane & 7) == 0 && bcol < pad_cols && r < pad_rows) {
-      const uint32_t word = code | (c1 << 8) | (c2 << 16) | (c3 << 24);
-      *reinterpret_cast<uint32_t*>(s + swz_offset(r, bcol, pad_cols)) = word;
+    const float amax = fmax_abs16(f);
+    const uint32_t code = ok ? block_code(amax, inv_g) : 0u;
+    const uint2 packed = encode16(f, inv_tab[code], amax);
+    if (ok) {
+      uint8_t* dst = q + r * (k >> 1) + 8 * c;
+      if (q8) {
+        *reinterpret_cast<uint2*>(dst) = packed;
+      } else {
+        reinterpret_cast<uint32_t*>(dst)[0] = packed.x;
+        reinterpret_cast<uint32_t*>(dst)[1] = packed.y;
+      }
     }
+    // the 4 codes of lanes 4i..4i+3 form one 32-bit word of the swizzled layout
+    const uint32_t c1 = __shfl_down_sync(0xffffffffu, code, 1);
+    const uint32_t c2 = __shfl_down_sync(0xffffffffu, code, 2);
+    const uint32_t c3 = __shfl_down_sync(0xffffffffu, code, 3);
+    if ((lane & 3) == 0 && c < pad_cols && r < pad_rows)
+      *reinterpret_cast<uint32_t*>(s + swz_offset(r, c, pad_cols)) = code | (c1 << 8) | (c2 << 16) | (c3 << 24);
   }
 }
 
-// Streaming 1/RMS for rows too wide to hold in registers (k > 8192): one
-// warp per row, same fp32 thread-sequential + butterfly order as above.
+// 1/RMS for rows too wide to hold in registers (k > 8192): one warp per row,
+// the same per-thread order and reduction tree as above.
 __global__ void __launch_bounds__(RMS_WARPS * 32) rms_inv_stream_kernel(
     const uint16_t* __restrict__ x, float* __restrict__ inv_rms, int64_t rows, int64_t k, float eps) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int64_t r = (int64_t)blockIdx.x * RMS_WARPS + wid;
   if (r >= rows) return;
-  float ss = 0.0f;
-  for (int64_t col = 8 * lane; col < k; col += 256) {
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + r * k + col));
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const int64_t nblk = k >> 4;
+  float ps[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float a0 = bf16lo(w[i]), a1 = bf16hi(w[i]);
-      ss += a0 * a0 + a1 * a1;
+  for (int m = 0; m < 8; ++m) ps[m] = 0.0f;
+  for (int64_t j0 = 0; 32 * j0 < nblk; j0 += 8) {
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const int64_t c = 32 * (j0 + m) + lane;
+      if (c < nblk) {
+        const uint4* p = reinterpret_cast<const uint4*>(x + r * k + 16 * c);
+        ps[m] = sumsq_block(ps[m], __ldg(p), __ldg(p + 1));
+      }
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (lane == 0) inv_rms[r] = rsqrtf(ss / (float)k + eps);
+  const float inv = rsqrtf((reduce_like_reference(ps) / (float)k) + eps);
+  if (lane == 0) inv_rms[r] = inv;
 }
 
 // ---------------------------------------------------------------------------
@@ -301,6 +386,7 @@ __global__ void __launch_bounds__(256) quant_t_kernel(
   uint16_t* tile = reinterpret_cast<uint16_t*>(smem_raw);                       // [TQ_T][TQ_STRIDE]
   uint8_t* s_tile = smem_raw + TQ_T * TQ_STRIDE * 2;                            // 2048 bytes
   float* rs_tile = reinterpret_cast<float*>(s_tile + 2048);                     // [TQ_T]
+  float* inv_tab = rs_tile + TQ_T;                                              // [256]
   const int tid = threadIdx.x;
   const int64_t t0 = (int64_t)blockIdx.x * TQ_T;
   const int64_t d0 = (int64_t)blockIdx.y * TQ_D;
@@ -316,10 +402,11 @@ __global__ void __launch_bounds__(256) quant_t_kernel(
     *reinterpret_cast<uint4*>(tile + t * TQ_STRIDE + dv) = val;
   }
   if (HAS_ROW) rs_tile[tid] = (t0 + tid < rows) ? __ldg(row_scale + t0 + tid) : 0.0f;
-  __syncthreads();
-
   const float g = load_global_scale(gptr);
   const float inv_g = __frcp_rn(g);
+  fill_inv_scale_table(inv_tab, g);
+  __syncthreads();
+
   const int p = tid & 63;          // d pair
   const int qtr = tid >> 6;        // blocks 4*qtr .. 4*qtr+3
   const int dl0 = 2 * p;
@@ -348,16 +435,14 @@ __global__ void __launch_bounds__(256) quant_t_kernel(
     float ama = 0.0f, amb = 0.0f;
 #pragma unroll
     for (int j = 0; j < 16; ++j) { ama = fmaxf(ama, fabsf(fa[j])); amb = fmaxf(amb, fabsf(fb[j])); }
-    float isa = 1.0f, isb = 1.0f;
-    const uint32_t ca = blk_ok ? block_scale(ama, g, inv_g, isa) : 0u;
-    const uint32_t cb = blk_ok ? block_scale(amb, g, inv_g, isb) : 0u;
-    float la[8], ha[8], lb[8], hb[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) { la[j] = fa[j]; ha[j] = fa[8 + j]; lb[j] = fb[j]; hb[j] = fb[8 + j]; }
-    qwa[2 * bi] = encode8(la, isa);
-    qwa[2 * bi + 1] = encode8(ha, isa);
-    qwb[2 * bi] = encode8(lb, isb);
-    qwb[2 * bi + 1] = encode8(hb, isb);
+    const uint32_t ca = blk_ok ? block_code(ama, inv_g) : 0u;
+    const uint32_t cb = blk_ok ? block_code(amb, inv_g) : 0u;
+    const uint2 pa = encode16(fa, inv_tab[ca], ama);
+    const uint2 pb = encode16(fb, inv_tab[cb], amb);
+    qwa[2 * bi] = pa.x;
+    qwa[2 * bi + 1] = pa.y;
+    qwb[2 * bi] = pb.x;
+    qwb[2 * bi + 1] = pb.y;
     codes_a |= ca << (8 * bi);
     codes_b |= cb << (8 * bi);
   }
@@ -393,7 +478,7 @@ __global__ void __launch_bounds__(256) quant_t_kernel(
     *reinterpret_cast<uint2*>(s + dst + tid * 8) = reinterpret_cast<const uint2*>(s_tile)[tid];
 }
 
-constexpr size_t TQ_SMEM = (size_t)TQ_T * TQ_STRIDE * 2 + 2048 + TQ_T * 4;
+constexpr size_t TQ_SMEM = (size_t)TQ_T * TQ_STRIDE * 2 + 2048 + TQ_T * 4 + 256 * 4;
 
 // ---------------------------------------------------------------------------
 // host launchers
@@ -407,14 +492,15 @@ static int launch_quant_tile(const void* x, const float* row_scale, const void* 
   auto gm = static_cast<const uint16_t*>(gamma);
   auto qq = static_cast<uint8_t*>(q);
   auto ss = static_cast<uint8_t*>(s);
+  const int q8 = aligned(q, 8) ? 1 : 0;
   if (row_scale && gamma)
-    quant_tile_kernel<true, true><<<grid, QT_THREADS, 0, st>>>(xs, row_scale, gm, qq, ss, rows, k, pad_cols, g);
+    quant_tile_kernel<true, true><<<grid, QT_THREADS, 0, st>>>(xs, row_scale, gm, qq, ss, rows, k, pad_cols, g, q8);
   else if (row_scale)
-    quant_tile_kernel<true, false><<<grid, QT_THREADS, 0, st>>>(xs, row_scale, gm, qq, ss, rows, k, pad_cols, g);
+    quant_tile_kernel<true, false><<<grid, QT_THREADS, 0, st>>>(xs, row_scale, gm, qq, ss, rows, k, pad_cols, g, q8);
   else if (gamma)
-    quant_tile_kernel<false, true><<<grid, QT_THREADS, 0, st>>>(xs, row_scale, gm, qq, ss, rows, k, pad_cols, g);
+    quant_tile_kernel<false, true><<<grid, QT_THREADS, 0, st>>>(xs, row_scale, gm, qq, ss, rows, k, pad_cols, g, q8);
   else
-    quant_tile_kernel<false, false><<<grid, QT_THREADS, 0, st>>>(xs, row_scale, gm, qq, ss, rows, k, pad_cols, g);
+    quant_tile_kernel<false, false><<<grid, QT_THREADS, 0, st>>>(xs, row_scale, gm, qq, ss, rows, k, pad_cols, g, q8);
   return launch_status();
 }
 
@@ -436,15 +522,16 @@ static int launch_rms_rows(const void* x, const void* gamma, void* q, void* s, f
   auto gm = static_cast<const uint16_t*>(gamma);
   auto qq = static_cast<uint8_t*>(q);
   auto ss = static_cast<uint8_t*>(s);
-  const int nv = (int)ceil_div(k, 256);
+  const int q8 = (q == nullptr || aligned(q, 8)) ? 1 : 0;
+  const int nv = (int)ceil_div(k, 512);
 #define NVFP4_RMS_CASE(NVV)                                                                       \
   if (nv <= NVV) {                                                                                \
     if (gamma)                                                                                    \
       rmsnorm_row_kernel<NVV, true, MODE><<<grid, RMS_WARPS * 32, 0, st>>>(                      \
-          xs, gm, qq, ss, inv_rms, rows, pad_rows, k, pad_cols, eps, g, ws, g_out);               \
+          xs, gm, qq, ss, inv_rms, rows, pad_rows, k, pad_cols, eps, g, ws, g_out, q8);           \
     else                                                                                          \
       rmsnorm_row_kernel<NVV, false, MODE><<<grid, RMS_WARPS * 32, 0, st>>>(                     \
-          xs, gm, qq, ss, inv_rms, rows, pad_rows, k, pad_cols, eps, g, ws, g_out);               \
+          xs, gm, qq, ss, inv_rms, rows, pad_rows, k, pad_cols, eps, g, ws, g_out, q8);           \
     return launch_status();                                                                       \
   }
   NVFP4_RMS_CASE(1)
@@ -452,7 +539,6 @@ static int launch_rms_rows(const void* x, const void* gamma, void* q, void* s, f
   NVFP4_RMS_CASE(4)
   NVFP4_RMS_CASE(8)
   NVFP4_RMS_CASE(16)
-  NVFP4_RMS_CASE(32)
 #undef NVFP4_RMS_CASE
   return NVFP4B200_ERR_BAD_SHAPE;
 }
