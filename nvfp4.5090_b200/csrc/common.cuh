@@ -21,6 +21,9 @@ namespace nvfp4b200 {
 // part (B200 family).  Cached per device; safe to call from many threads.
 int check_device();
 
+// Returns and clears the quantizer kernels' device error word (0 if none).
+int take_quant_device_error();
+
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 inline int launch_status() {

@@ -781,6 +781,9 @@ int nvfp4b200_get_device_error(int* out) {
   if (cudaDeviceSynchronize() != cudaSuccess) return NVFP4B200_ERR_CUDA;
   if (cudaMemcpyFromSymbol(out, g_device_error, sizeof(int)) != cudaSuccess) return NVFP4B200_ERR_CUDA;
   if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)) != cudaSuccess) return NVFP4B200_ERR_CUDA;
+  const int qe = take_quant_device_error();
+  if (qe == NVFP4B200_ERR_CUDA) return qe;
+  if (*out == 0) *out = qe;
   return NVFP4B200_OK;
 }
 

@@ -193,9 +193,9 @@ __global__ void __launch_bounds__(QT_THREADS) quant_tile_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// fused RMSNorm -> quantize: one warp per row, the row held in registers
+// fused RMSNorm -> quantize: reduction helpers
 // ---------------------------------------------------------------------------
-// Lane L of the warp owns the 16-element blocks c = 32 j + L (chunk j of 512
+// One warp handles a row; lane L of the warp owns the 16-element blocks c = 32 j + L (chunk j of 512
 // columns).  The sum of squares reproduces the reference's fp32 order exactly
 // (float4utils.py:183-222, 256 threads per row): thread t accumulates
 // ``sum_sq += a0 * a0 + a1 * a1`` over its blocks t, t + 256, ... word by
@@ -235,115 +235,8 @@ __device__ __forceinline__ float reduce_like_reference(float (&ps)[8]) {
   return __shfl_sync(0xffffffffu, total, 0);
 }
 
-// MODE 0: quantize (computes inv_rms, writes it).  MODE 1: statistics only
-// (inv_rms + global amax of the normalised row).
-template <int NV, bool HAS_GAMMA, int MODE>
-__global__ void __launch_bounds__(RMS_WARPS * 32) rmsnorm_row_kernel(
-    const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma, uint8_t* __restrict__ q,
-    uint8_t* __restrict__ s, float* __restrict__ inv_rms_out, int64_t rows, int64_t pad_rows,
-    int64_t k, int64_t pad_cols, float eps, const float* __restrict__ gptr, uint32_t* ws,
-    float* g_out, int q8) {
-  __shared__ float inv_tab[256];
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int64_t r = (int64_t)blockIdx.x * RMS_WARPS + wid;
-  const bool row_ok = r < rows;
-  const int64_t nblk = k >> 4;
-  float g = 1.0f, inv_g = 1.0f;
-  if (MODE == 0) {
-    g = load_global_scale(gptr);
-    inv_g = __frcp_rn(g);
-    fill_inv_scale_table(inv_tab, g);
-    __syncthreads();
-  }
-  uint4 v[NV][2];
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int64_t c = 32 * j + lane;
-    v[j][0] = make_uint4(0, 0, 0, 0);
-    v[j][1] = v[j][0];
-    if (row_ok && c < nblk) {
-      const uint4* p = reinterpret_cast<const uint4*>(x + r * k + 16 * c);
-      v[j][0] = __ldg(p);
-      v[j][1] = __ldg(p + 1);
-    }
-  }
-  float ps[8];
-#pragma unroll
-  for (int m = 0; m < 8; ++m) ps[m] = 0.0f;
-#pragma unroll
-  for (int j = 0; j < NV; ++j) ps[j & 7] = sumsq_block(ps[j & 7], v[j][0], v[j][1]);
-  const float inv = rsqrtf((reduce_like_reference(ps) / (float)k) + eps);
-  if (row_ok && lane == 0 && inv_rms_out) inv_rms_out[r] = inv;
-
-  if (MODE == 1) {
-    float am = 0.0f;
-    if (row_ok) {
-#pragma unroll
-      for (int j = 0; j < NV; ++j) {
-        const int64_t c = 32 * j + lane;
-        if (c >= nblk) continue;
-        uint32_t w[8];
-        float f[16];
-        unpack16(v[j][0], v[j][1], w, f);
-        float gam[16];
-        if (HAS_GAMMA) {
-          const uint4* gp = reinterpret_cast<const uint4*>(gamma + 16 * c);
-          uint32_t gw[8];
-          unpack16(__ldg(gp), __ldg(gp + 1), gw, gam);
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float a = f[i] * inv;
-          if (HAS_GAMMA) a = a * gam[i];
-          am = fmaxf(am, fabsf(a));
-        }
-      }
-    }
-    amax_commit(__float_as_uint(am), ws, g_out, nullptr);
-    return;
-  }
-
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int64_t c = 32 * j + lane;              // block column of this lane
-    if (32 * j >= pad_cols) continue;             // whole chunk beyond the padded scale columns
-    const bool ok = row_ok && c < nblk;
-    uint32_t w[8];
-    float f[16];
-    unpack16(v[j][0], v[j][1], w, f);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) f[i] = f[i] * inv;
-    if (HAS_GAMMA && ok) {
-      const uint4* gp = reinterpret_cast<const uint4*>(gamma + 16 * c);
-      uint32_t gw[8];
-      float gam[16];
-      unpack16(__ldg(gp), __ldg(gp + 1), gw, gam);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) f[i] = f[i] * gam[i];
-    }
-    const float amax = fmax_abs16(f);
-    const uint32_t code = ok ? block_code(amax, inv_g) : 0u;
-    const uint2 packed = encode16(f, inv_tab[code], amax);
-    if (ok) {
-      uint8_t* dst = q + r * (k >> 1) + 8 * c;
-      if (q8) {
-        *reinterpret_cast<uint2*>(dst) = packed;
-      } else {
-        reinterpret_cast<uint32_t*>(dst)[0] = packed.x;
-        reinterpret_cast<uint32_t*>(dst)[1] = packed.y;
-      }
-    }
-    // the 4 codes of lanes 4i..4i+3 form one 32-bit word of the swizzled layout
-    const uint32_t c1 = __shfl_down_sync(0xffffffffu, code, 1);
-    const uint32_t c2 = __shfl_down_sync(0xffffffffu, code, 2);
-    const uint32_t c3 = __shfl_down_sync(0xffffffffu, code, 3);
-    if ((lane & 3) == 0 && c < pad_cols && r < pad_rows)
-      *reinterpret_cast<uint32_t*>(s + swz_offset(r, c, pad_cols)) = code | (c1 << 8) | (c2 << 16) | (c3 << 24);
-  }
-}
-
-// 1/RMS for rows too wide to hold in registers (k > 8192): one warp per row,
-// the same per-thread order and reduction tree as above.
+// 1/RMS for rows wider than the row kernel covers (k > 16384): one warp per row,
+// the same per-thread order and reduction tree.
 __global__ void __launch_bounds__(RMS_WARPS * 32) rms_inv_stream_kernel(
     const uint16_t* __restrict__ x, float* __restrict__ inv_rms, int64_t rows, int64_t k, float eps) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -365,6 +258,145 @@ __global__ void __launch_bounds__(RMS_WARPS * 32) rms_inv_stream_kernel(
   }
   const float inv = rsqrtf((reduce_like_reference(ps) / (float)k) + eps);
   if (lane == 0) inv_rms[r] = inv;
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm rows: one CTA per row, the reference's thread layout
+// ---------------------------------------------------------------------------
+// Thread t of a CTA owns the blocks c = t, t + 256, ... of the row, exactly
+// as the reference kernel (float4utils.py:169-295, 256 threads per row), so
+// the sum of squares, the per-warp shfl_down tree and the cross-warp tree are
+// the reference's own and 1/RMS is bit-identical.  CTAs are persistent and
+// keep the next row's loads in flight in registers while the current row is
+// reduced and quantized.  A CTA has min(256, padded blocks) threads; threads
+// the reference has beyond that hold no blocks and add zeros to the trees.
+// Every thread keeps its blocks' floats between the reduction and the
+// quantization.  Block codes of threads 4i..4i+3 form one 32-bit word of the
+// swizzled scale layout.
+
+__device__ int g_quant_error = 0;
+
+template <int BPT, bool HAS_GAMMA, int MODE>
+__global__ void __launch_bounds__(256) rmsnorm_cta_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma, uint8_t* __restrict__ q,
+    uint8_t* __restrict__ s, float* __restrict__ inv_rms_out, int64_t rows, int64_t pad_rows, int64_t k,
+    int64_t pad_cols, float eps, const float* __restrict__ gptr, uint32_t* ws, float* g_out, int q8) {
+  __shared__ float warp_sum[8];
+  __shared__ float row_inv;
+  __shared__ float inv_tab[256];
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int64_t nblk = k >> 4;
+  const int64_t cover = MODE == 0 ? pad_rows : rows;
+  float g = 1.0f, inv_g = 1.0f;
+  if (MODE == 0) {
+    g = load_global_scale(gptr);
+    inv_g = __frcp_rn(g);
+    fill_inv_scale_table(inv_tab, g);
+  }
+  float gam[BPT][16];
+  if (HAS_GAMMA) {
+#pragma unroll
+    for (int b = 0; b < BPT; ++b) {
+      const int64_t c = t + 256 * b;
+      uint4 g0 = make_uint4(0, 0, 0, 0), g1 = g0;
+      if (c < nblk) {
+        const uint4* gp = reinterpret_cast<const uint4*>(gamma + 16 * c);
+        g0 = __ldg(gp);
+        g1 = __ldg(gp + 1);
+      }
+      uint32_t gw[8];
+      unpack16(g0, g1, gw, gam[b]);
+    }
+  }
+  auto load_row = [&](int64_t r, uint4 (&buf)[BPT][2]) {
+#pragma unroll
+    for (int b = 0; b < BPT; ++b) {
+      const int64_t c = t + 256 * b;
+      buf[b][0] = make_uint4(0, 0, 0, 0);
+      buf[b][1] = buf[b][0];
+      if (r < rows && c < nblk) {
+        const uint4* p = reinterpret_cast<const uint4*>(x + r * k + 16 * c);
+        buf[b][0] = __ldg(p);
+        buf[b][1] = __ldg(p + 1);
+      }
+    }
+  };
+  float am = 0.0f;  // MODE 1: running |normalised| max of this thread
+  uint4 cur[BPT][2], nxt[BPT][2];
+  int64_t r = blockIdx.x;
+  load_row(r, cur);
+  __syncthreads();  // inv_tab
+  for (; r < cover; r += gridDim.x) {
+    load_row(r + gridDim.x, nxt);
+    if (r >= rows) {  // padding row of the scale tensor: zero codes
+      for (int64_t c = 4 * t; c < pad_cols; c += 4 * blockDim.x)
+        *reinterpret_cast<uint32_t*>(s + swz_offset(r, c, pad_cols)) = 0u;
+      continue;
+    }
+    float f[BPT][16];
+    float ss = 0.0f;
+#pragma unroll
+    for (int b = 0; b < BPT; ++b) {
+      uint32_t w[8];
+      unpack16(cur[b][0], cur[b][1], w, f[b]);
+      if (t + 256 * b < nblk) ss = sumsq_block(ss, cur[b][0], cur[b][1]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_down_sync(0xffffffffu, ss, off);
+    if (lane == 0) warp_sum[wid] = ss;
+    __syncthreads();
+    if (wid == 0) {
+      float v = (lane < nwarps) ? warp_sum[lane] : 0.0f;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_down_sync(0xffffffffu, v, off);
+      if (lane == 0) {
+        const float inv = rsqrtf((v / (float)k) + eps);
+        row_inv = inv;
+        if (inv_rms_out) inv_rms_out[r] = inv;
+      }
+    }
+    __syncthreads();
+    const float inv = row_inv;
+#pragma unroll
+    for (int b = 0; b < BPT; ++b) {
+      const int64_t c = t + 256 * b;
+      const bool in = c < nblk;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) f[b][e] = f[b][e] * inv;
+      if (HAS_GAMMA) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) f[b][e] = f[b][e] * gam[b][e];
+      }
+      const float amax = in ? fmax_abs16(f[b]) : 0.0f;
+      if (MODE == 1) {
+        am = fmaxf(am, amax);
+        continue;
+      }
+      const uint32_t code = in ? block_code(amax, inv_g) : 0u;
+      const uint2 packed = encode16(f[b], inv_tab[code], amax);
+      if (in) {
+        uint8_t* dst = q + r * (k >> 1) + 8 * c;
+        if (q8) {
+          *reinterpret_cast<uint2*>(dst) = packed;
+        } else {
+          reinterpret_cast<uint32_t*>(dst)[0] = packed.x;
+          reinterpret_cast<uint32_t*>(dst)[1] = packed.y;
+        }
+      }
+      const uint32_t c1 = __shfl_down_sync(0xffffffffu, code, 1);
+      const uint32_t c2 = __shfl_down_sync(0xffffffffu, code, 2);
+      const uint32_t c3 = __shfl_down_sync(0xffffffffu, code, 3);
+      if ((lane & 3) == 0 && c < pad_cols)
+        *reinterpret_cast<uint32_t*>(s + swz_offset(r, c, pad_cols)) = code | (c1 << 8) | (c2 << 16) | (c3 << 24);
+    }
+#pragma unroll
+    for (int b = 0; b < BPT; ++b) {
+      cur[b][0] = nxt[b][0];
+      cur[b][1] = nxt[b][1];
+    }
+  }
+  if (MODE == 1) amax_commit(__float_as_uint(am), ws, g_out, nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -512,35 +544,43 @@ static int check_quant_args(const void* x, const void* q, const void* s, int64_t
 }
 
 template <int MODE>
-static int launch_rms_rows(const void* x, const void* gamma, void* q, void* s, float* inv_rms,
-                           int64_t rows, int64_t k, float eps, const float* g, uint32_t* ws,
-                           float* g_out, cudaStream_t st) {
+static int launch_rms_cta(const void* x, const void* gamma, void* q, void* s, float* inv_rms, int64_t rows, int64_t k,
+                          float eps, const float* g, uint32_t* ws, float* g_out, cudaStream_t st) {
   const int64_t pad_rows = round_up(rows, 128), pad_cols = round_up(k / 16, 4);
   const int64_t cover = MODE == 0 ? pad_rows : rows;
-  dim3 grid((unsigned)std::max<int64_t>(1, ceil_div(cover, RMS_WARPS)));
-  auto xs = static_cast<const uint16_t*>(x);
-  auto gm = static_cast<const uint16_t*>(gamma);
-  auto qq = static_cast<uint8_t*>(q);
-  auto ss = static_cast<uint8_t*>(s);
+  const int64_t span = MODE == 0 ? pad_cols : k / 16;  // blocks a CTA must cover
+  const int bpt = (int)ceil_div(span, 256);
+  const int threads = (int)std::min<int64_t>(256, round_up(span, 32));
   const int q8 = (q == nullptr || aligned(q, 8)) ? 1 : 0;
-  const int nv = (int)ceil_div(k, 512);
-#define NVFP4_RMS_CASE(NVV)                                                                       \
-  if (nv <= NVV) {                                                                                \
-    if (gamma)                                                                                    \
-      rmsnorm_row_kernel<NVV, true, MODE><<<grid, RMS_WARPS * 32, 0, st>>>(                      \
-          xs, gm, qq, ss, inv_rms, rows, pad_rows, k, pad_cols, eps, g, ws, g_out, q8);           \
-    else                                                                                          \
-      rmsnorm_row_kernel<NVV, false, MODE><<<grid, RMS_WARPS * 32, 0, st>>>(                     \
-          xs, gm, qq, ss, inv_rms, rows, pad_rows, k, pad_cols, eps, g, ws, g_out, q8);           \
-    return launch_status();                                                                       \
-  }
+  auto run = [&](auto kern) -> int {
+    int per_sm = 0, dev = 0, sms = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0) != cudaSuccess || per_sm < 1)
+      return NVFP4B200_ERR_CUDA;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(cover, (int64_t)sms * per_sm));
+    kern<<<(unsigned)grid, threads, 0, st>>>(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gamma),
+                                             static_cast<uint8_t*>(q), static_cast<uint8_t*>(s), inv_rms, rows,
+                                             pad_rows, k, pad_cols, eps, g, ws, g_out, q8);
+    return launch_status();
+  };
+#define NVFP4_RMS_CASE(B)                                                         \
+  if (bpt <= B)                                                                   \
+    return gamma ? run(rmsnorm_cta_kernel<B, true, MODE>) : run(rmsnorm_cta_kernel<B, false, MODE>);
   NVFP4_RMS_CASE(1)
   NVFP4_RMS_CASE(2)
   NVFP4_RMS_CASE(4)
-  NVFP4_RMS_CASE(8)
-  NVFP4_RMS_CASE(16)
 #undef NVFP4_RMS_CASE
   return NVFP4B200_ERR_BAD_SHAPE;
+}
+
+static bool rms_cta_fits(int64_t k) { return round_up(k / 16, 4) <= 4 * 256; }
+
+int take_quant_device_error() {
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_quant_error, sizeof(int)) != cudaSuccess) return NVFP4B200_ERR_CUDA;
+  if (v && cudaMemcpyToSymbol(g_quant_error, &zero, sizeof(int)) != cudaSuccess) return NVFP4B200_ERR_CUDA;
+  return v;
 }
 
 }  // namespace nvfp4b200
@@ -597,8 +637,8 @@ int nvfp4b200_rmsnorm_quant_nvfp4(const void* x, const void* gamma, void* q, voi
   if ((rc = check_device())) return rc;
   if (rows == 0) return NVFP4B200_OK;
   cudaStream_t st = (cudaStream_t)stream;
-  if (k <= 32 * 256)
-    return launch_rms_rows<0>(x, gamma, q, s, inv_rms, rows, k, eps, global_scale, nullptr, nullptr, st);
+  if (rms_cta_fits(k))
+    return launch_rms_cta<0>(x, gamma, q, s, inv_rms, rows, k, eps, global_scale, nullptr, nullptr, st);
   // wide rows: 1/RMS pass, then the scaled tile quantizer reads x again
   rms_inv_stream_kernel<<<(unsigned)ceil_div(rows, RMS_WARPS), RMS_WARPS * 32, 0, st>>>(
       static_cast<const uint16_t*>(x), inv_rms, rows, k, eps);
@@ -610,12 +650,12 @@ int nvfp4b200_rmsnorm_quant_nvfp4(const void* x, const void* gamma, void* q, voi
 int nvfp4b200_rmsnorm_stats(const void* x, const void* gamma, float* inv_rms, int64_t rows, int64_t k,
                             float eps, uint32_t* ws, float* global_scale_out, void* stream) {
   if (!x || !inv_rms || !ws || !global_scale_out) return NVFP4B200_ERR_INVALID_ARG;
-  if (rows <= 0 || k <= 0 || k % 16 || k > 32 * 256) return NVFP4B200_ERR_BAD_SHAPE;
+  if (rows <= 0 || k <= 0 || k % 16 || !rms_cta_fits(k)) return NVFP4B200_ERR_BAD_SHAPE;
   if (!aligned(x, 16) || (gamma && !aligned(gamma, 16)) || !aligned(ws, 4)) return NVFP4B200_ERR_MISALIGNED;
   int rc = check_device();
   if (rc) return rc;
-  return launch_rms_rows<1>(x, gamma, nullptr, nullptr, inv_rms, rows, k, eps, nullptr, ws,
-                            global_scale_out, (cudaStream_t)stream);
+  return launch_rms_cta<1>(x, gamma, nullptr, nullptr, inv_rms, rows, k, eps, nullptr, ws, global_scale_out,
+                           (cudaStream_t)stream);
 }
 
 int nvfp4b200_quant_nvfp4_t(const void* x, const float* row_scale, const void* gamma, void* q, void* s,
