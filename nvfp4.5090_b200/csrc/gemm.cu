@@ -204,6 +204,13 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                "r"(x), "r"(y)
                : "memory");
 }
+// 2-D tiled TMA reduce-add of a shared-memory box into global memory (the
+// element type, f32 here, comes from the tensor map; L2 performs the add).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // This thread's bulk stores have finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
@@ -348,25 +355,6 @@ __device__ __forceinline__ void finish64(uint32_t* v, const Params& p, float alp
   }
 }
 
-__device__ __forceinline__ void store_f32_64(const uint32_t* v, const Params& p, int64_t row, int64_t col0) {
-  float* dst = static_cast<float*>(p.d) + row * p.ldd + col0;
-#pragma unroll
-  for (int i4 = 0; i4 < 16; ++i4) {
-    if (col0 + 4 * i4 < p.n) {
-      float4 o = make_float4(__uint_as_float(v[4 * i4]), __uint_as_float(v[4 * i4 + 1]),
-                             __uint_as_float(v[4 * i4 + 2]), __uint_as_float(v[4 * i4 + 3]));
-      if (p.accumulate) {
-        const float4 old = reinterpret_cast<const float4*>(dst)[i4];
-        o.x += old.x;
-        o.y += old.y;
-        o.z += old.z;
-        o.w += old.w;
-      }
-      reinterpret_cast<float4*>(dst)[i4] = o;
-    }
-  }
-}
-
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
@@ -410,7 +398,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     prefetch_tmap(&tmap_b);
     prefetch_tmap(&tmap_sfa);
     prefetch_tmap(&tmap_sfb);
-    if (!p.d_f32) prefetch_tmap(&tmap_d);
+    prefetch_tmap(&tmap_d);
   }
   if (warp == 1) {
     tmem_alloc2(smem_u32(tmem_slot), TMEM_COLS);
@@ -604,6 +592,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           }
         }
       } else {
+        // f32: each 32-row x 32-column piece (4 KB) goes through the staging
+        // buffer and out with one TMA store, or with a TMA reduce-add when
+        // accumulating (D += result, the add done in L2; no read of D here).
+        const uint32_t obuf = smem_u32(sOut + (warp - 2) * OUT_CHUNK_BYTES);
+        const uint32_t orow = obuf + lane * 128;
+        const int y0 = mb * TILE_M + (int)rank * CTA_M + quad * 32;
 #pragma unroll 1
         for (int r = 0; r < 2; ++r) {
           const int c = r ^ first;
@@ -618,7 +612,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             if (lane == 0) mbar_arrive_cluster(leader_overlap_free);
           }
           finish64(acc, p, alpha, row, colbase + c * 64, row_ok);
-          if (row_ok) store_f32_64(acc, p, row, colbase + c * 64);
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            if (lane == 0) bulk_wait_read();
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              st_shared_v4(orow + ((j ^ (lane & 7)) << 4), acc[32 * hh + 4 * j], acc[32 * hh + 4 * j + 1],
+                           acc[32 * hh + 4 * j + 2], acc[32 * hh + 4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            const int64_t x0 = colbase + c * 64 + 32 * hh;  // element column (the f32 map counts elements)
+            if (lane == 0 && y0 < p.m && x0 < p.n) {
+              if (p.accumulate)
+                tma_reduce_add_2d(&tmap_d, obuf, (int)x0, y0);
+              else
+                tma_store_2d(&tmap_d, obuf, (int)x0, y0);
+              bulk_commit();
+            }
+          }
         }
       }
     }
@@ -654,6 +666,20 @@ static EncodeTiledFn encode_fn() {
       fn = reinterpret_cast<EncodeTiledFn>(ptr);
   });
   return fn;
+}
+
+// 2-D f32 tensor [rows, cols] (row stride ld elements) with box {32, 32} and
+// 128-byte swizzle: the output map of f32 results (store and reduce-add).
+static bool make_map_f32(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // 2-D byte tensor [rows, row_bytes] with box {box_x bytes, box_rows}.
@@ -739,6 +765,7 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   // bf16 output viewed as bytes: [m rows, 2n bytes], row stride 2*ldd, boxes of 32 rows x 128 bytes
   if (d_dtype == NVFP4B200_BF16 && !make_map(&md, d, m, 2 * n, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B, 2 * ldd))
     return NVFP4B200_ERR_CUDA;
+  if (d_dtype == NVFP4B200_F32 && !make_map_f32(&md, d, m, n, ldd)) return NVFP4B200_ERR_CUDA;
   Params p;
   p.scale_a = scale_a;
   p.scale_b = scale_b;

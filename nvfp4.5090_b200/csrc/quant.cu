@@ -12,6 +12,8 @@
 // the scale tensor is needed.
 #include "common.cuh"
 
+#include <cuda.h>
+
 #include <algorithm>
 #include <mutex>
 
@@ -402,119 +404,220 @@ __global__ void __launch_bounds__(256) rmsnorm_cta_kernel(
 // ---------------------------------------------------------------------------
 // transposed quantizer: x [rows, cols] -> quantize x^T along rows
 // ---------------------------------------------------------------------------
+// Persistent CTAs walk 128 x 128 input tiles (input rows t0.., input columns
+// d0..).  Thread 0 keeps the next tile's TMA load (and its 128 row scales)
+// in flight into the other half of a double buffer while all 256 threads
+// encode the current one: thread (qtr, p) owns output rows d0 + 2p, 2p + 1
+// (input columns) and the blocks 2 qtr, 2 qtr + 1 of the tile (input rows
+// t0 + 32 qtr .. + 32), reads its column pair down the tile (a warp reads 128
+// contiguous bytes of a tile row) and writes 16 bytes of nibbles per output
+// row.  The tile's 2 scale atoms (1 KB) are staged in shared memory and
+// written whole.  Waits are bounded; a timeout sets g_quant_error.
 
-__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+constexpr int TQ_T = 128;                  // input rows per tile = output k extent (8 blocks)
+constexpr int TQ_D = 128;                  // input columns per tile = output rows
+constexpr int TQ_TILE_BYTES = TQ_T * TQ_D * 2;
+constexpr long long TQ_WAIT_LIMIT = 4000000000LL;
 
-constexpr int TQ_T = 256;          // input rows per CTA = output k extent (16 blocks)
-constexpr int TQ_D = 128;          // input cols per CTA = output rows (one atom group)
-constexpr int TQ_STRIDE = TQ_D + 8;  // smem row stride in bf16 (272 bytes)
+struct TqSmem {
+  uint16_t tile[2][TQ_T * TQ_D];
+  float rs[2][TQ_T];
+  uint8_t atoms[2][2 * 512];
+  float inv_tab[256];
+  uint64_t full[2];
+};
+
+__device__ __forceinline__ uint32_t tq_smem(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ bool tq_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 
 template <bool HAS_ROW, bool HAS_GAMMA>
 __global__ void __launch_bounds__(256) quant_t_kernel(
-    const uint16_t* __restrict__ x, const float* __restrict__ row_scale,
-    const uint16_t* __restrict__ gamma, uint8_t* __restrict__ q, uint8_t* __restrict__ s,
-    int64_t rows, int64_t cols, int64_t pad_cols_out, const float* __restrict__ gptr) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  uint16_t* tile = reinterpret_cast<uint16_t*>(smem_raw);                       // [TQ_T][TQ_STRIDE]
-  uint8_t* s_tile = smem_raw + TQ_T * TQ_STRIDE * 2;                            // 2048 bytes
-  float* rs_tile = reinterpret_cast<float*>(s_tile + 2048);                     // [TQ_T]
-  float* inv_tab = rs_tile + TQ_T;                                              // [256]
+    const __grid_constant__ CUtensorMap xmap, const float* __restrict__ row_scale,
+    const uint16_t* __restrict__ gamma, uint8_t* __restrict__ q, uint8_t* __restrict__ s, int64_t rows,
+    int64_t cols, int64_t pad_cols_out, int n_tiles_t, int n_tiles, const float* __restrict__ gptr, int q16) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  TqSmem& sm = *reinterpret_cast<TqSmem*>(smem_raw);
   const int tid = threadIdx.x;
-  const int64_t t0 = (int64_t)blockIdx.x * TQ_T;
-  const int64_t d0 = (int64_t)blockIdx.y * TQ_D;
-
-  // load 256 x 128 bf16 (16 uint4 per row, 16 rows per pass of 256 threads)
-#pragma unroll 4
-  for (int it = 0; it < 16; ++it) {
-    const int t = it * 16 + (tid >> 4);
-    const int dv = (tid & 15) * 8;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (t0 + t < rows && d0 + dv < cols)
-      val = __ldg(reinterpret_cast<const uint4*>(x + (t0 + t) * cols + d0 + dv));
-    *reinterpret_cast<uint4*>(tile + t * TQ_STRIDE + dv) = val;
-  }
-  if (HAS_ROW) rs_tile[tid] = (t0 + tid < rows) ? __ldg(row_scale + t0 + tid) : 0.0f;
+  const int p = tid & 63;      // column pair
+  const int qtr = tid >> 6;    // blocks 2 qtr, 2 qtr + 1
+  const int dl0 = 2 * p;
   const float g = load_global_scale(gptr);
   const float inv_g = __frcp_rn(g);
-  fill_inv_scale_table(inv_tab, g);
-  __syncthreads();
+  fill_inv_scale_table(sm.inv_tab, g);
 
-  const int p = tid & 63;          // d pair
-  const int qtr = tid >> 6;        // blocks 4*qtr .. 4*qtr+3
-  const int dl0 = 2 * p;
-  float gam0 = 1.0f, gam1 = 1.0f;
-  if (HAS_GAMMA) {
-    if (d0 + dl0 < cols) gam0 = __uint_as_float((uint32_t)gamma[d0 + dl0] << 16);
-    if (d0 + dl0 + 1 < cols) gam1 = __uint_as_float((uint32_t)gamma[d0 + dl0 + 1] << 16);
-  }
-  uint32_t codes_a = 0, codes_b = 0;
-  uint32_t qwa[8], qwb[8];   // packed nibbles: 4 blocks x 8 bytes for each of the two output rows
-#pragma unroll
-  for (int bi = 0; bi < 4; ++bi) {
-    const int b = qtr * 4 + bi;
-    float fa[16], fb[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int t = b * 16 + j;
-      const uint32_t w = *reinterpret_cast<const uint32_t*>(tile + t * TQ_STRIDE + dl0);
-      float a = bf16lo(w), c = bf16hi(w);
-      if (HAS_ROW) { const float rsv = rs_tile[t]; a = a * rsv; c = c * rsv; }
-      if (HAS_GAMMA) { a = a * gam0; c = c * gam1; }
-      fa[j] = a;
-      fb[j] = c;
+  auto issue = [&](int tile, int buf) {  // thread 0
+    const int64_t t0 = (int64_t)(tile % n_tiles_t) * TQ_T;
+    const int64_t d0 = (int64_t)(tile / n_tiles_t) * TQ_D;
+    const uint32_t bar = tq_smem(&sm.full[buf]);
+    uint32_t bytes = TQ_TILE_BYTES;
+    int64_t nrs = 0;
+    if (HAS_ROW) {
+      nrs = imin64(TQ_T, rows - t0);
+      if (nrs > 0) bytes += (uint32_t)(nrs * 4);
     }
-    const bool blk_ok = t0 + b * 16 < rows;
-    float ama = 0.0f, amb = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) { ama = fmaxf(ama, fabsf(fa[j])); amb = fmaxf(amb, fabsf(fb[j])); }
-    const uint32_t ca = blk_ok ? block_code(ama, inv_g) : 0u;
-    const uint32_t cb = blk_ok ? block_code(amb, inv_g) : 0u;
-    const uint2 pa = encode16(fa, inv_tab[ca], ama);
-    const uint2 pb = encode16(fb, inv_tab[cb], amb);
-    qwa[2 * bi] = pa.x;
-    qwa[2 * bi + 1] = pa.y;
-    qwb[2 * bi] = pb.x;
-    qwb[2 * bi + 1] = pb.y;
-    codes_a |= ca << (8 * bi);
-    codes_b |= cb << (8 * bi);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            tq_smem(sm.tile[buf])),
+        "l"(&xmap), "r"((int)d0), "r"((int)t0), "r"(bar)
+        : "memory");
+    if (HAS_ROW && nrs > 0)
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       tq_smem(sm.rs[buf])),
+                   "l"(row_scale + t0), "r"((uint32_t)(nrs * 4)), "r"(bar)
+                   : "memory");
+  };
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tq_smem(&sm.full[0])) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tq_smem(&sm.full[1])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
+    if ((int)blockIdx.x < n_tiles) issue(blockIdx.x, 0);
+    if ((int)blockIdx.x + (int)gridDim.x < n_tiles) issue(blockIdx.x + gridDim.x, 1);
   }
-  // output rows d0+dl0 and d0+dl0+1; 32 bytes each at column (t0 + 64*qtr)/2
-  const int64_t kout = rows;
-  const int64_t tcol = t0 + 64 * qtr;
-  if (tcol < rows) {
-    // rows/2 is a multiple of 8, so an output row start is 8-byte aligned;
-    // 16-byte stores only when the whole 32 bytes are in range and aligned.
-    const int64_t nbytes = imin64(32, (rows - tcol) >> 1);
-    const uint32_t* qw[2] = {qwa, qwb};
+  __syncthreads();  // barriers initialised, inv_tab filled
+
+  bool ok = true;
+  int it = 0;
+  for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+    const int buf = it & 1;
+    const int64_t t0 = (int64_t)(tile % n_tiles_t) * TQ_T;
+    const int64_t d0 = (int64_t)(tile / n_tiles_t) * TQ_D;
+    {
+      const uint32_t bar = tq_smem(&sm.full[buf]);
+      const uint32_t par = (uint32_t)((it >> 1) & 1);
+      bool done = tq_try_wait(bar, par);
+      const long long w0 = clock64();
+      while (!done && clock64() - w0 < TQ_WAIT_LIMIT) done = tq_try_wait(bar, par);
+      ok = __syncthreads_and(done);
+      if (!ok) break;
+    }
+    const uint16_t* tl = sm.tile[buf];
+    float gam0 = 1.0f, gam1 = 1.0f;
+    if (HAS_GAMMA) {
+      if (d0 + dl0 < cols) gam0 = __uint_as_float((uint32_t)gamma[d0 + dl0] << 16);
+      if (d0 + dl0 + 1 < cols) gam1 = __uint_as_float((uint32_t)gamma[d0 + dl0 + 1] << 16);
+    }
+    uint32_t qwa[4], qwb[4];
+    uint32_t codes_a = 0, codes_b = 0;
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      if (d0 + dl0 + h >= cols) continue;
-      uint8_t* dst = q + (d0 + dl0 + h) * (kout >> 1) + (tcol >> 1);
-      if (nbytes == 32 && aligned16(dst)) {
-        reinterpret_cast<uint4*>(dst)[0] = make_uint4(qw[h][0], qw[h][1], qw[h][2], qw[h][3]);
-        reinterpret_cast<uint4*>(dst)[1] = make_uint4(qw[h][4], qw[h][5], qw[h][6], qw[h][7]);
-      } else {
-        for (int i = 0; i < nbytes / 8; ++i)
-          reinterpret_cast<uint2*>(dst)[i] = make_uint2(qw[h][2 * i], qw[h][2 * i + 1]);
+    for (int bi = 0; bi < 2; ++bi) {
+      const int b = 2 * qtr + bi;
+      float fa[16], fb[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int t = b * 16 + j;
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(tl + t * TQ_D + dl0);
+        float a = bf16lo(w), c = bf16hi(w);
+        if (HAS_ROW) {
+          const float rsv = sm.rs[buf][t];
+          a = a * rsv;
+          c = c * rsv;
+        }
+        if (HAS_GAMMA) {
+          a = a * gam0;
+          c = c * gam1;
+        }
+        fa[j] = a;
+        fb[j] = c;
+      }
+      const bool blk_ok = t0 + b * 16 < rows;   // rows % 16 == 0: a block is all in or all out
+      const float ama = fmax_abs16(fa), amb = fmax_abs16(fb);
+      const uint32_t ca = blk_ok ? block_code(ama, inv_g) : 0u;
+      const uint32_t cb = blk_ok ? block_code(amb, inv_g) : 0u;
+      const uint2 pa = encode16(fa, sm.inv_tab[ca], ama);
+      const uint2 pb = encode16(fb, sm.inv_tab[cb], amb);
+      qwa[2 * bi] = pa.x;
+      qwa[2 * bi + 1] = pa.y;
+      qwb[2 * bi] = pb.x;
+      qwb[2 * bi + 1] = pb.y;
+      codes_a |= ca << (8 * bi);
+      codes_b |= cb << (8 * bi);
+    }
+    __syncthreads();  // every thread is done reading this buffer
+    if (tid == 0 && tile + 2 * (int)gridDim.x < n_tiles) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(tile + 2 * gridDim.x, buf);
+    }
+    // nibbles: output rows d0 + dl0 (+1), 16 bytes at byte column (t0 + 32 qtr) / 2
+    const int64_t tcol = t0 + 32 * qtr;
+    if (tcol < rows) {
+      const int64_t nbytes = imin64(16, (rows - tcol) >> 1);   // 16 or 8 (rows % 16 == 0)
+      const uint32_t* qw[2] = {qwa, qwb};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (d0 + dl0 + h >= cols) continue;
+        uint8_t* dst = q + (d0 + dl0 + h) * (rows >> 1) + (tcol >> 1);
+        if (nbytes == 16 && q16) {
+          *reinterpret_cast<uint4*>(dst) = make_uint4(qw[h][0], qw[h][1], qw[h][2], qw[h][3]);
+        } else {
+          reinterpret_cast<uint2*>(dst)[0] = make_uint2(qw[h][0], qw[h][1]);
+          if (nbytes == 16) reinterpret_cast<uint2*>(dst)[1] = make_uint2(qw[h][2], qw[h][3]);
+        }
       }
     }
+    // scale codes: output row dl, blocks 2 qtr, 2 qtr + 1 = atom qtr / 2, columns (2 qtr) % 4 + 0, 1
+    uint8_t* at = sm.atoms[buf] + (qtr >> 1) * 512;
+    const int c0 = (2 * qtr) & 3;
+    *reinterpret_cast<uint16_t*>(at + atom_offset(dl0, c0)) = (uint16_t)((d0 + dl0 < cols) ? codes_a : 0u);
+    *reinterpret_cast<uint16_t*>(at + atom_offset(dl0 + 1, c0)) = (uint16_t)((d0 + dl0 + 1 < cols) ? codes_b : 0u);
+    __syncthreads();
+    const int64_t atom0 = (int64_t)(tile % n_tiles_t) * 2;
+    const int64_t n_atoms = imin64(2, (pad_cols_out >> 2) - atom0);
+    const int64_t dst = ((int64_t)(tile / n_tiles_t) * (pad_cols_out >> 2) + atom0) * 512;
+    if ((int64_t)tid * 4 < n_atoms * 512)
+      *reinterpret_cast<uint32_t*>(s + dst + tid * 4) = reinterpret_cast<const uint32_t*>(sm.atoms[buf])[tid];
   }
-  // scale codes: output row dl, blocks 4*qtr..4*qtr+3 = atom qtr, columns 0..3
-  *reinterpret_cast<uint32_t*>(s_tile + qtr * 512 + atom_offset(dl0, 0)) = (d0 + dl0 < cols) ? codes_a : 0u;
-  *reinterpret_cast<uint32_t*>(s_tile + qtr * 512 + atom_offset(dl0 + 1, 0)) = (d0 + dl0 + 1 < cols) ? codes_b : 0u;
-  __syncthreads();
-  const int64_t atom0 = (int64_t)blockIdx.x * 4;
-  const int64_t n_atoms = imin64(4, (pad_cols_out >> 2) - atom0);
-  const int64_t dst = ((int64_t)blockIdx.y * (pad_cols_out >> 2) + atom0) * 512;
-  if ((int64_t)tid * 8 < n_atoms * 512)
-    *reinterpret_cast<uint2*>(s + dst + tid * 8) = reinterpret_cast<const uint2*>(s_tile)[tid];
+  if (!ok && tid == 0) {
+    atomicExch(&g_quant_error, NVFP4B200_ERR_TIMEOUT);
+    const long long w0 = clock64();  // let loads still in flight land before the CTA exits
+    for (int b = 0; b < 2; ++b)
+      for (uint32_t par = 0; par < 2; ++par)
+        while (!tq_try_wait(tq_smem(&sm.full[b]), par) && clock64() - w0 < TQ_WAIT_LIMIT) {
+        }
+  }
 }
-
-constexpr size_t TQ_SMEM = (size_t)TQ_T * TQ_STRIDE * 2 + 2048 + TQ_T * 4 + 256 * 4;
 
 // ---------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFnQ)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// 2-D bf16 tensor [rows, cols] (row stride cols) with box {box_cols, box_rows},
+// no swizzle; loads outside the tensor read zeros.
+static bool make_bf16_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_cols, int box_rows) {
+  static EncodeTiledFnQ fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFnQ>(ptr);
+  });
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 
 static int launch_quant_tile(const void* x, const float* row_scale, const void* gamma, void* q,
                              void* s, int64_t rows, int64_t k, const float* g, cudaStream_t st) {
@@ -662,31 +765,39 @@ int nvfp4b200_quant_nvfp4_t(const void* x, const float* row_scale, const void* g
                             int64_t rows, int64_t cols, const float* global_scale, void* stream) {
   if (!x || !q || !s) return NVFP4B200_ERR_INVALID_ARG;
   if (rows <= 0 || cols <= 0 || rows % 16 || cols % 8) return NVFP4B200_ERR_BAD_SHAPE;
+  if (rows > (1ll << 31) - TQ_T || cols > (1ll << 31) - TQ_D) return NVFP4B200_ERR_BAD_SHAPE;
   if (!aligned(x, 16) || !aligned(q, 16) || !aligned(s, 16)) return NVFP4B200_ERR_MISALIGNED;
   if (gamma && !aligned(gamma, 2)) return NVFP4B200_ERR_MISALIGNED;
+  if (row_scale && !aligned(row_scale, 16)) return NVFP4B200_ERR_MISALIGNED;
   int rc = check_device();
   if (rc) return rc;
   const int64_t pad_rows_out = round_up(cols, 128), pad_cols_out = round_up(rows / 16, 4);
-  dim3 grid((unsigned)ceil_div(pad_cols_out * 16, TQ_T), (unsigned)(pad_rows_out / TQ_D));
+  const int64_t n_tiles_t = ceil_div(pad_cols_out * 16, TQ_T), n_tiles_d = pad_rows_out / TQ_D;
+  if (n_tiles_t * n_tiles_d > (1ll << 31) - 1) return NVFP4B200_ERR_BAD_SHAPE;
+  CUtensorMap xmap;
+  if (!make_bf16_map(&xmap, x, rows, cols, TQ_D, TQ_T)) return NVFP4B200_ERR_CUDA;
   cudaStream_t st = (cudaStream_t)stream;
-  auto xs = static_cast<const uint16_t*>(x);
-  auto gm = static_cast<const uint16_t*>(gamma);
-  auto qq = static_cast<uint8_t*>(q);
-  auto ss = static_cast<uint8_t*>(s);
-#define NVFP4_TQ(HR, HG)                                                                        \
-  {                                                                                             \
-    if (cudaFuncSetAttribute(quant_t_kernel<HR, HG>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                             (int)TQ_SMEM) != cudaSuccess)                                      \
-      return NVFP4B200_ERR_CUDA;                                                                \
-    quant_t_kernel<HR, HG><<<grid, 256, TQ_SMEM, st>>>(xs, row_scale, gm, qq, ss, rows, cols,  \
-                                                       pad_cols_out, global_scale);             \
-  }
-  if (row_scale && gamma) NVFP4_TQ(true, true)
-  else if (row_scale) NVFP4_TQ(true, false)
-  else if (gamma) NVFP4_TQ(false, true)
-  else NVFP4_TQ(false, false)
-#undef NVFP4_TQ
-  return launch_status();
+  const int q16 = ((rows >> 1) % 16 == 0) ? 1 : 0;
+  const int n_tiles = (int)(n_tiles_t * n_tiles_d);
+  auto run = [&](auto kern) -> int {
+    const int smem = (int)sizeof(TqSmem);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return NVFP4B200_ERR_CUDA;
+    int per_sm = 0, dev = 0, sms = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem) != cudaSuccess || per_sm < 1)
+      return NVFP4B200_ERR_CUDA;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = (int)std::min<int64_t>(n_tiles, (int64_t)sms * per_sm);
+    kern<<<grid, 256, smem, st>>>(xmap, row_scale, static_cast<const uint16_t*>(gamma), static_cast<uint8_t*>(q),
+                                  static_cast<uint8_t*>(s), rows, cols, pad_cols_out, (int)n_tiles_t, n_tiles,
+                                  global_scale, q16);
+    return launch_status();
+  };
+  if (row_scale && gamma) return run(quant_t_kernel<true, true>);
+  if (row_scale) return run(quant_t_kernel<true, false>);
+  if (gamma) return run(quant_t_kernel<false, true>);
+  return run(quant_t_kernel<false, false>);
 }
 
 int nvfp4b200_global_scale(const void* x, int64_t n, uint32_t* ws, float* global_scale_out,

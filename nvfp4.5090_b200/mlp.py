@@ -262,11 +262,9 @@ class NVFP4MLPStackTrainer:
                     g = block_backward(g, b.gamma, qws[bi], saved[bi], b.grad_gamma32, b.grad_gu, b.grad_down,
                                        accumulate=False)
                 else:
-                    if mi == 0:
-                        b.acc_gu.zero_()
-                        b.acc_down.zero_()
+                    # the first micro-batch writes the fp32 accumulators, later ones add to them
                     g = block_backward(g, b.gamma, qws[bi], saved[bi], b.grad_gamma32, b.acc_gu, b.acc_down,
-                                       accumulate=True)
+                                       accumulate=mi > 0)
                     if last:
                         b.grad_gu.copy_(b.acc_gu)
                         b.grad_down.copy_(b.acc_down)

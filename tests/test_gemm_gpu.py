@@ -134,6 +134,24 @@ def test_gemm_f32_accumulate_and_residual(pkg):
     assert orc.rel_frobenius(dr.float().cpu().numpy(), want) < 1e-2
 
 
+def test_gemm_f32_strided_output_store_then_reduce_add(pkg):
+    """fp32 results go out through TMA stores (overwrite) and TMA reduce-adds
+    (accumulate) into a column window of a wider matrix; the columns around
+    the window stay untouched."""
+    m, n, k = 300, 520, 256
+    qa, sa, qb, sb = make(pkg, m, n, k, seed=9)
+    ref = orc.gemm_emulation_f64(u8(qa), u8(sa), u8(qb), u8(sb), m, n, k)
+    big = torch.full((m, 1024), -7.0, device="cuda", dtype=torch.float32)
+    out = big[:, 8:8 + n]
+    pkg.ops.gemm(qa, sa, qb, sb, out=out)
+    pkg.ops.gemm(qa, sa, qb, sb, out=out, accumulate=True)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().astype(np.float64)
+    assert np.all(np.abs(got - 2 * ref) <= 2e-4 * np.abs(ref) + 2e-4)
+    rest = torch.cat([big[:, :8], big[:, 8 + n:]], dim=1)
+    assert torch.all(rest == -7.0)
+
+
 def test_gemm_8192_cubed_sampled(pkg):
     """Headline GEMM size: check 256 sampled output elements against float64."""
     m = n = k = 8192
