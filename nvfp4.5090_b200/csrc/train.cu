@@ -23,7 +23,9 @@ static unsigned grid_for(int64_t work_items, int threads, int per_sm = 8) {
   return (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sm_count() * per_sm));
 }
 
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+// sigmoid with the fast exponential and division intrinsics; 0 for x -> -inf
+// (the division returns 0 when the denominator is infinite), 1 for x -> +inf.
+__device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
@@ -37,27 +39,29 @@ __device__ __forceinline__ uint32_t absmax_word_bits(uint32_t w) {
   return max(a & 0xFFFFu, a >> 16) << 16;
 }
 
-// h = silu(gate) * up, 8 columns per thread; optional global amax of h.
+// h = silu(gate) * up with gu = [gate | up] per row; optional global amax of
+// h.  CTAs stride over rows, threads over 8-column vectors of a row.
 __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const uint16_t* __restrict__ gu, uint16_t* __restrict__ h,
                                                          int64_t tokens, int64_t ff, uint32_t* ws, float* g_out) {
-  const int64_t vec_per_row = ff / 8;
-  const int64_t total = tokens * vec_per_row;
   uint32_t m = 0;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = i / vec_per_row, c = (i - t * vec_per_row) * 8;
-    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gu + t * 2 * ff + c));
-    const uint4 uv = __ldg(reinterpret_cast<const uint4*>(gu + t * 2 * ff + ff + c));
-    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
-    uint32_t o[4];
+  for (int64_t t = blockIdx.x; t < tokens; t += gridDim.x) {
+    const uint16_t* grow = gu + t * 2 * ff;
+    uint16_t* hrow = h + t * ff;
+    for (int64_t c = 8 * (int64_t)threadIdx.x; c < ff; c += 8 * (int64_t)blockDim.x) {
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(grow + c));
+      const uint4 uv = __ldg(reinterpret_cast<const uint4*>(grow + ff + c));
+      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+      uint32_t o[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float g0 = bf16lo(gw[j]), g1 = bf16hi(gw[j]);
-      const float h0 = g0 * sigmoidf_(g0) * bf16lo(uw[j]);
-      const float h1 = g1 * sigmoidf_(g1) * bf16hi(uw[j]);
-      o[j] = pack2(h0, h1);
-      m = max(m, absmax_word_bits(o[j]));
+      for (int j = 0; j < 4; ++j) {
+        const float g0 = bf16lo(gw[j]), g1 = bf16hi(gw[j]);
+        const float h0 = g0 * sigmoidf_(g0) * bf16lo(uw[j]);
+        const float h1 = g1 * sigmoidf_(g1) * bf16hi(uw[j]);
+        o[j] = pack2(h0, h1);
+        m = max(m, absmax_word_bits(o[j]));
+      }
+      *reinterpret_cast<uint4*>(hrow + c) = make_uint4(o[0], o[1], o[2], o[3]);
     }
-    *reinterpret_cast<uint4*>(h + t * ff + c) = make_uint4(o[0], o[1], o[2], o[3]);
   }
   if (ws) amax_commit(m, ws, g_out, nullptr);
 }
@@ -67,44 +71,47 @@ __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const uint16_t* __restr
 __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint16_t* __restrict__ gu,
                                                          const uint16_t* __restrict__ dh, uint16_t* __restrict__ dgu,
                                                          int64_t tokens, int64_t ff, uint32_t* ws, float* g_out) {
-  const int64_t vec_per_row = ff / 8;
-  const int64_t total = tokens * vec_per_row;
   uint32_t m = 0;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = i / vec_per_row, c = (i - t * vec_per_row) * 8;
-    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gu + t * 2 * ff + c));
-    const uint4 uv = __ldg(reinterpret_cast<const uint4*>(gu + t * 2 * ff + ff + c));
-    const uint4 dv = __ldg(reinterpret_cast<const uint4*>(dh + t * ff + c));
-    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w},
-                   dw[4] = {dv.x, dv.y, dv.z, dv.w};
-    uint32_t og[4], ou[4];
+  for (int64_t t = blockIdx.x; t < tokens; t += gridDim.x) {
+    const uint16_t* grow = gu + t * 2 * ff;
+    const uint16_t* drow = dh + t * ff;
+    uint16_t* orow = dgu + t * 2 * ff;
+    for (int64_t c = 8 * (int64_t)threadIdx.x; c < ff; c += 8 * (int64_t)blockDim.x) {
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(grow + c));
+      const uint4 uv = __ldg(reinterpret_cast<const uint4*>(grow + ff + c));
+      const uint4 dv = __ldg(reinterpret_cast<const uint4*>(drow + c));
+      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w},
+                     dw[4] = {dv.x, dv.y, dv.z, dv.w};
+      uint32_t og[4], ou[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float dg[2], du[2];
+      for (int j = 0; j < 4; ++j) {
+        float dg[2], du[2];
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float g = e ? bf16hi(gw[j]) : bf16lo(gw[j]);
-        const float u = e ? bf16hi(uw[j]) : bf16lo(uw[j]);
-        const float d = e ? bf16hi(dw[j]) : bf16lo(dw[j]);
-        const float s = sigmoidf_(g);
-        du[e] = d * (g * s);
-        dg[e] = d * u * (s * (1.0f + g * (1.0f - s)));
+        for (int e = 0; e < 2; ++e) {
+          const float g = e ? bf16hi(gw[j]) : bf16lo(gw[j]);
+          const float u = e ? bf16hi(uw[j]) : bf16lo(uw[j]);
+          const float d = e ? bf16hi(dw[j]) : bf16lo(dw[j]);
+          const float sg = sigmoidf_(g);
+          du[e] = d * (g * sg);
+          dg[e] = d * u * (sg * (1.0f + g * (1.0f - sg)));
+        }
+        og[j] = pack2(dg[0], dg[1]);
+        ou[j] = pack2(du[0], du[1]);
+        m = max(m, max(absmax_word_bits(og[j]), absmax_word_bits(ou[j])));
       }
-      og[j] = pack2(dg[0], dg[1]);
-      ou[j] = pack2(du[0], du[1]);
-      m = max(m, max(absmax_word_bits(og[j]), absmax_word_bits(ou[j])));
+      *reinterpret_cast<uint4*>(orow + c) = make_uint4(og[0], og[1], og[2], og[3]);
+      *reinterpret_cast<uint4*>(orow + ff + c) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
     }
-    *reinterpret_cast<uint4*>(dgu + t * 2 * ff + c) = make_uint4(og[0], og[1], og[2], og[3]);
-    *reinterpret_cast<uint4*>(dgu + t * 2 * ff + ff + c) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
   }
   if (ws) amax_commit(m, ws, g_out, nullptr);
 }
 
-// RMSNorm backward.  One CTA (256 threads) walks a band of rows; thread t
-// owns columns {2048*v + 8*t + i}.  Per row: s = sum(dy*gamma*xn) by a
-// block reduction, dx = inv*(dy*gamma - xn*s/k) + dres; dgamma partial sums
-// stay in registers for the whole band and are added to global once.
-constexpr int RB_THREADS = 256;
+// RMSNorm backward.  Persistent CTAs of 512 threads walk a band of rows;
+// thread t owns columns {4096 v + 8 t + i}.  The next row's x and dy are
+// loaded while the current row is reduced.  Per row: s = sum(dy*gamma*xn)
+// (block reduction), dx = inv*(dy*gamma - xn*s/k) + dres; dgamma partial
+// sums stay in registers for the band and are added to global once.
+constexpr int RB_THREADS = 512;
 template <int NV>
 __global__ void __launch_bounds__(RB_THREADS) rmsnorm_bwd_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma, const float* __restrict__ inv_rms,
@@ -115,7 +122,7 @@ __global__ void __launch_bounds__(RB_THREADS) rmsnorm_bwd_kernel(
   float gam[NV][8], dgam[NV][8];
 #pragma unroll
   for (int v = 0; v < NV; ++v) {
-    const int64_t col = (int64_t)v * 2048 + 8 * tid;
+    const int64_t col = (int64_t)v * 4096 + 8 * tid;
     uint4 gv = make_uint4(0, 0, 0, 0);
     if (col < k) gv = gamma ? __ldg(reinterpret_cast<const uint4*>(gamma + col))
                             : make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
@@ -130,48 +137,57 @@ __global__ void __launch_bounds__(RB_THREADS) rmsnorm_bwd_kernel(
   }
   const int64_t r_begin = (int64_t)blockIdx.x * rows_per_cta;
   const int64_t r_end = imin64(rows, r_begin + rows_per_cta);
+  auto load = [&](int64_t r, uint4 (&xv)[NV], uint4 (&dv)[NV]) {
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int64_t col = (int64_t)v * 4096 + 8 * tid;
+      xv[v] = make_uint4(0, 0, 0, 0);
+      dv[v] = xv[v];
+      if (r < r_end && col < k) {
+        xv[v] = __ldg(reinterpret_cast<const uint4*>(x + r * k + col));
+        dv[v] = __ldg(reinterpret_cast<const uint4*>(dy + r * k + col));
+      }
+    }
+  };
+  uint4 cx[NV], cd[NV], nx[NV], nd[NV];
+  load(r_begin, cx, cd);
   int buf = 0;
   for (int64_t r = r_begin; r < r_end; ++r) {
+    load(r + 1, nx, nd);
     const float inv = __ldg(inv_rms + r);
-    float xn[NV][8], dyg[NV][8];
     float part = 0.0f;
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
-      const int64_t col = (int64_t)v * 2048 + 8 * tid;
-      uint4 xv = make_uint4(0, 0, 0, 0), dv = make_uint4(0, 0, 0, 0);
-      if (col < k) {
-        xv = __ldg(reinterpret_cast<const uint4*>(x + r * k + col));
-        dv = __ldg(reinterpret_cast<const uint4*>(dy + r * k + col));
-      }
-      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
+      const uint32_t xw[4] = {cx[v].x, cx[v].y, cx[v].z, cx[v].w}, dw[4] = {cd[v].x, cd[v].y, cd[v].z, cd[v].w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        xn[v][2 * j] = bf16lo(xw[j]) * inv;
-        xn[v][2 * j + 1] = bf16hi(xw[j]) * inv;
-        const float d0 = bf16lo(dw[j]), d1 = bf16hi(dw[j]);
-        dgam[v][2 * j] += d0 * xn[v][2 * j];
-        dgam[v][2 * j + 1] += d1 * xn[v][2 * j + 1];
-        dyg[v][2 * j] = d0 * gam[v][2 * j];
-        dyg[v][2 * j + 1] = d1 * gam[v][2 * j + 1];
-        part += dyg[v][2 * j] * xn[v][2 * j] + dyg[v][2 * j + 1] * xn[v][2 * j + 1];
+      for (int j = 0; j < 8; ++j) {
+        const float xn = (j & 1 ? bf16hi(xw[j >> 1]) : bf16lo(xw[j >> 1])) * inv;
+        const float d = j & 1 ? bf16hi(dw[j >> 1]) : bf16lo(dw[j >> 1]);
+        dgam[v][j] += d * xn;
+        part += (d * gam[v][j]) * xn;
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
     if (lane == 0) red[buf][wid] = part;
     __syncthreads();
-    float s = 0.0f;
+    float sum = 0.0f;
 #pragma unroll
-    for (int i = 0; i < RB_THREADS / 32; ++i) s += red[buf][i];
+    for (int i = 0; i < RB_THREADS / 32; ++i) sum += red[buf][i];
     buf ^= 1;
-    const float mean = s / (float)k;
+    const float mean = sum / (float)k;
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
-      const int64_t col = (int64_t)v * 2048 + 8 * tid;
+      const int64_t col = (int64_t)v * 4096 + 8 * tid;
       if (col >= k) continue;
+      const uint32_t xw[4] = {cx[v].x, cx[v].y, cx[v].z, cx[v].w}, dw[4] = {cd[v].x, cd[v].y, cd[v].z, cd[v].w};
       float o[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = inv * (dyg[v][j] - xn[v][j] * mean);
+      for (int j = 0; j < 8; ++j) {
+        const float xn = (j & 1 ? bf16hi(xw[j >> 1]) : bf16lo(xw[j >> 1])) * inv;
+        const float d = j & 1 ? bf16hi(dw[j >> 1]) : bf16lo(dw[j >> 1]);
+        o[j] = inv * (d * gam[v][j] - xn * mean);
+      }
       if (dres) {
         const uint4 rv = __ldg(reinterpret_cast<const uint4*>(dres + r * k + col));
         const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
@@ -184,11 +200,16 @@ __global__ void __launch_bounds__(RB_THREADS) rmsnorm_bwd_kernel(
       *reinterpret_cast<uint4*>(dx + r * k + col) =
           make_uint4(pack2(o[0], o[1]), pack2(o[2], o[3]), pack2(o[4], o[5]), pack2(o[6], o[7]));
     }
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      cx[v] = nx[v];
+      cd[v] = nd[v];
+    }
   }
   if (dgamma) {
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
-      const int64_t col = (int64_t)v * 2048 + 8 * tid;
+      const int64_t col = (int64_t)v * 4096 + 8 * tid;
       if (col >= k) continue;
 #pragma unroll
       for (int j = 0; j < 8; ++j) atomicAdd(dgamma + col + j, dgam[v][j]);
@@ -286,7 +307,7 @@ int nvfp4b200_swiglu_fwd(const void* gu, void* h, int64_t tokens, int64_t ff, ui
   int rc = check_device();
   if (rc) return rc;
   if (tokens == 0) return NVFP4B200_OK;
-  swiglu_fwd_kernel<<<grid_for(tokens * ff / 8, 256), 256, 0, (cudaStream_t)stream>>>(
+  swiglu_fwd_kernel<<<(unsigned)std::min<int64_t>(tokens, (int64_t)sm_count() * 8), 256, 0, (cudaStream_t)stream>>>(
       static_cast<const uint16_t*>(gu), static_cast<uint16_t*>(h), tokens, ff, ws, global_scale_out);
   return launch_status();
 }
@@ -300,7 +321,7 @@ int nvfp4b200_swiglu_bwd(const void* gu, const void* dh, void* dgu, int64_t toke
   int rc = check_device();
   if (rc) return rc;
   if (tokens == 0) return NVFP4B200_OK;
-  swiglu_bwd_kernel<<<grid_for(tokens * ff / 8, 256), 256, 0, (cudaStream_t)stream>>>(
+  swiglu_bwd_kernel<<<(unsigned)std::min<int64_t>(tokens, (int64_t)sm_count() * 8), 256, 0, (cudaStream_t)stream>>>(
       static_cast<const uint16_t*>(gu), static_cast<const uint16_t*>(dh), static_cast<uint16_t*>(dgu), tokens, ff, ws,
       global_scale_out);
   return launch_status();
@@ -309,14 +330,15 @@ int nvfp4b200_swiglu_bwd(const void* gu, const void* dh, void* dgu, int64_t toke
 int nvfp4b200_rmsnorm_bwd(const void* x, const void* gamma, const float* inv_rms, const void* dy, const void* dres,
                           void* dx, float* dgamma_acc, int64_t rows, int64_t k, void* stream) {
   if (!x || !inv_rms || !dy || !dx) return NVFP4B200_ERR_INVALID_ARG;
-  if (rows < 0 || k <= 0 || k % 8 || k > 4 * 2048) return NVFP4B200_ERR_BAD_SHAPE;
+  if (rows < 0 || k <= 0 || k % 8 || k > 2 * 4096) return NVFP4B200_ERR_BAD_SHAPE;
   if (!aligned(x, 16) || !aligned(dy, 16) || !aligned(dx, 16) || (gamma && !aligned(gamma, 16)) ||
       (dres && !aligned(dres, 16)) || !aligned(inv_rms, 4))
     return NVFP4B200_ERR_MISALIGNED;
   int rc = check_device();
   if (rc) return rc;
   if (rows == 0) return NVFP4B200_OK;
-  const int64_t ctas = std::min<int64_t>(rows, (int64_t)sm_count() * 4);
+  // one resident CTA per SM at k > 4096 (128 registers x 512 threads), two below
+  const int64_t ctas = std::min<int64_t>(rows, (int64_t)sm_count() * (k > 4096 ? 1 : 2));
   const int64_t rpc = ceil_div(rows, ctas);
   const unsigned grid = (unsigned)ceil_div(rows, rpc);
   cudaStream_t st = (cudaStream_t)stream;
@@ -325,13 +347,10 @@ int nvfp4b200_rmsnorm_bwd(const void* x, const void* gamma, const float* inv_rms
   auto DY = static_cast<const uint16_t*>(dy);
   auto DR = static_cast<const uint16_t*>(dres);
   auto DX = static_cast<uint16_t*>(dx);
-  const int nv = (int)ceil_div(k, 2048);
-  if (nv <= 1)
+  if (k <= 4096)
     rmsnorm_bwd_kernel<1><<<grid, RB_THREADS, 0, st>>>(X, G, inv_rms, DY, DR, DX, dgamma_acc, rows, k, rpc);
-  else if (nv <= 2)
-    rmsnorm_bwd_kernel<2><<<grid, RB_THREADS, 0, st>>>(X, G, inv_rms, DY, DR, DX, dgamma_acc, rows, k, rpc);
   else
-    rmsnorm_bwd_kernel<4><<<grid, RB_THREADS, 0, st>>>(X, G, inv_rms, DY, DR, DX, dgamma_acc, rows, k, rpc);
+    rmsnorm_bwd_kernel<2><<<grid, RB_THREADS, 0, st>>>(X, G, inv_rms, DY, DR, DX, dgamma_acc, rows, k, rpc);
   return launch_status();
 }
 
