@@ -299,7 +299,47 @@ def bench_gemm(pkg, args, world, rank, peaks):
                   "path": "nvfp4b200_nvfp4_mm C ABI (gn_kernels::cutlass_sm120a_nvfp4_mm contract)"}
     # correctness spot check against float64 (a few elements)
     res["spot_check_max_rel_err"] = gemm_spot_check(qa, sa, qb, sb, out, ga, gb)
+    # M sweep at N = K = 8192 (same B operand), ours and cuBLASLt, L2 flushed per launch
+    if rank == 0 and not args.no_sweep:
+        res["m_sweep"] = gemm_m_sweep(pkg, args, qb, sb, gb, flush, with_cublas=not args.no_cublas)
     return res
+
+
+def gemm_m_sweep(pkg, args, qb, sb, gb, flush, with_cublas=True):
+    import torch
+    out = {}
+    n, k = qb.shape[0], 2 * qb.shape[1]
+    for m in (128, 1024, 16384):
+        g = torch.Generator(device="cuda").manual_seed(100 + m)
+        a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+        ga = pkg.ops.global_scale(a)
+        qa, sa = pkg.ops.quantize(a, global_scale=ga)
+        del a
+        d = torch.empty((m, n), device="cuda", dtype=torch.bfloat16)
+        run = lambda: pkg.ops.gemm(qa, sa, qb, sb, scale_a=ga, scale_b=gb, out=d)
+        for _ in range(3):
+            run()
+        t = timed_launches(run, max(args.steps, 5), flush)
+        ms = sum(t) / len(t)
+        row = {"M": m, "N": n, "K": k, "ms": ms, "tflops": 2.0 * m * n * k / (ms * 1e-3) / 1e12}
+        if with_cublas:
+            try:
+                import torch.nn.functional as F
+                from torch.nn.functional import ScalingType, SwizzleType
+                cub = lambda: F.scaled_mm(qa.view(torch.float4_e2m1fn_x2), qb.view(torch.float4_e2m1fn_x2).mT,
+                                          sa.view(torch.float8_e4m3fn), ScalingType.BlockWise1x16,
+                                          sb.view(torch.float8_e4m3fn), ScalingType.BlockWise1x16,
+                                          swizzle_a=SwizzleType.SWIZZLE_32_4_4, swizzle_b=SwizzleType.SWIZZLE_32_4_4,
+                                          output_dtype=torch.bfloat16, contraction_dim=(1, 0))
+                for _ in range(3):
+                    cub()
+                ct = timed_launches(cub, max(args.steps, 5), flush)
+                row["cublaslt_tflops"] = 2.0 * m * n * k / (sum(ct) / len(ct) * 1e-3) / 1e12
+            except Exception as e:  # keep the sweep even if the library path is unavailable
+                row["cublaslt_error"] = f"{type(e).__name__}: {str(e)[:120]}"
+        out[str(m)] = row
+        del qa, sa, d
+    return out
 
 
 def gemm_spot_check(qa, sa, qb, sb, out, ga, gb):
@@ -389,6 +429,7 @@ def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=No
         e0.record()
         for _ in range(args.steps):
             r = trainer.step(x, dy)
+        trainer.finish()   # the last step's parameter gathers (ZeRO-1 at N > 1)
         e1.record()
         torch.cuda.synchronize()
         barrier(world)
@@ -409,6 +450,7 @@ def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=No
         ddy.copy_(hdy, non_blocking=True)
         r = trainer.step(dx, ddy)
         hres.copy_(r, non_blocking=True)
+    trainer.finish()
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / max(1, args.steps // 2)
@@ -480,6 +522,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip", default="", help="comma list of sub-benchmarks to skip: quant,mlp_block,mlp_stack,cpu")
     ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the GEMM M sweep")
     ap.add_argument("--no-clock-hold", action="store_true", help="skip the 1 s sustained clock window (profiling)")
     ap.add_argument("--only", choices=["gemm", "quant", "mlp_block", "mlp_stack"], default=None,
                     help="run one section and print its result (profiling runs)")
@@ -535,6 +578,8 @@ def main(argv=None):
             "gpu_launches": args.steps * gemm["gpu_launches_per_step"],
             "cublaslt_scaled_mm_tflops": gemm.get("cublaslt_scaled_mm_tflops"),
             "spot_check_max_rel_err": gemm["spot_check_max_rel_err"]}
+    if "m_sweep" in gemm:
+        line["gemm_m_sweep"] = gemm["m_sweep"]
     if "cublaslt_error" in gemm:
         line["cublaslt_error"] = gemm["cublaslt_error"]
     if rank == 0 and world == 1 and "cpu" not in skip:
@@ -550,7 +595,9 @@ def main(argv=None):
     if "mlp_stack" not in skip:
         line["mlp_stack"] = bench_mlp(pkg, args, world, rank, 8, 8192, 28672, 65536, seed=4, pg=pg)
         line["mlp_stack"]["workload"] = ("8 RMSNorm+SwiGLU blocks, d=8192, ff=28672, 65536 global tokens split "
-                                         "across ranks, bf16 wgrad all-reduce (NCCL) overlapped with backward")
+                                         "across ranks; at N > 1 ZeRO-1: bf16 wgrad reduce-scatter (NCCL) overlapped "
+                                         "with backward, AdamW on each rank's 1/N shard, bf16 parameter all-gather "
+                                         "overlapped with the next step's forward")
         line["mlp_stack"]["scaling"] = "strong"
     if rank == 0:
         print(json.dumps(line), flush=True)

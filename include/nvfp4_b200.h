@@ -53,6 +53,15 @@ int nvfp4b200_device_check(void);
  * they give up (synchronises the current device).  *out = 0 when none. */
 int nvfp4b200_get_device_error(int* out);
 
+/* Caps the number of SMs the persistent GEMM kernel occupies on every device
+ * (0 = all SMs, the default; values are rounded down to whole CTA pairs,
+ * minimum one pair).  Process-wide.  A data-parallel training step lowers it
+ * so that collective kernels (NCCL all-reduce of the gradient buckets) find
+ * free SMs while GEMMs run, instead of waiting for them to finish.  No
+ * counterpart in the reference (its GEMM is a library call).  Returns
+ * NVFP4B200_ERR_INVALID_ARG for negative values. */
+int nvfp4b200_set_gemm_max_sms(int max_sms);
+
 /* ------------------------------------------------------------------------ */
 /* Quantizers                                                               */
 /* ------------------------------------------------------------------------ */

@@ -45,6 +45,7 @@
 #include <cuda.h>
 #include <algorithm>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 namespace nvfp4b200 {
@@ -701,6 +702,9 @@ struct DeviceInfo {
   int max_clusters = 0;
 };
 
+// Process-wide cap on the SMs a GEMM launch occupies (0 = no cap).
+static std::atomic<int> g_gemm_max_sms{0};
+
 static DeviceInfo device_info() {
   static std::mutex mu;
   static DeviceInfo cache[64];
@@ -785,7 +789,10 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   p.epilogue = epilogue;
   const int64_t tiles = (int64_t)p.num_m_tiles * p.num_n_tiles;
   const DeviceInfo info = device_info();
-  const int clusters = (int)std::min<int64_t>(tiles, info.max_clusters);
+  int cap = info.max_clusters;
+  const int max_sms = g_gemm_max_sms.load(std::memory_order_relaxed);
+  if (max_sms > 0) cap = std::max(1, std::min(cap, max_sms / 2));
+  const int clusters = (int)std::min<int64_t>(tiles, cap);
   if (cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
       cudaSuccess)
     return NVFP4B200_ERR_CUDA;
@@ -811,6 +818,12 @@ int nvfp4b200_get_device_error(int* out) {
   const int qe = take_quant_device_error();
   if (qe == NVFP4B200_ERR_CUDA) return qe;
   if (*out == 0) *out = qe;
+  return NVFP4B200_OK;
+}
+
+int nvfp4b200_set_gemm_max_sms(int max_sms) {
+  if (max_sms < 0) return NVFP4B200_ERR_INVALID_ARG;
+  gemm::g_gemm_max_sms.store(max_sms, std::memory_order_relaxed);
   return NVFP4B200_OK;
 }
 

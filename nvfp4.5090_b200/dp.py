@@ -1,12 +1,21 @@
 """Data-parallel plumbing of the NVFP4 MLP training step.
 
-The token dimension is sharded across ranks (one process per GPU); weights
-are replicated and every rank re-quantizes the same bf16 weights, so the only
-exchange is the bf16 weight-gradient all-reduce.  It runs over NCCL (NVLink /
-NVSwitch) through torch.distributed, one bucket per MLP block, launched as
-soon as that block's wgrad GEMMs are enqueued so the transfer overlaps the
-backward of the blocks below.  The reference has no distributed code; this
-module is new.
+The token dimension is sharded across ranks (one process per GPU); every
+rank holds the bf16 weights and re-quantizes them, so the only exchanges are
+on the weight gradients.  Two schemes, both over NCCL (NVLink / NVSwitch)
+through torch.distributed with one bucket per MLP block, launched as soon as
+that block's wgrad GEMMs are enqueued so the transfer overlaps the backward
+of the blocks below:
+
+* ``BucketAllReducer``: SUM all-reduce of each gradient bucket; every rank
+  then runs the full optimizer update.
+* ``ShardedBucketOptimizer`` (ZeRO-1): reduce-scatter of each bucket, the
+  optimizer update of this rank's 1/world shard only (optimizer state exists
+  only for the shard), then an all-gather of the updated parameter shards.
+  The per-step optimizer work and memory then fall as 1/world; the gathers
+  are waited for lazily, right before a block's weights are next used.
+
+The reference has no distributed code; this module is new.
 """
 from __future__ import annotations
 
@@ -72,6 +81,98 @@ class BucketAllReducer:
     def wait_all(self) -> None:
         for k in list(self.works):
             self.wait(k)
+
+    def grad_scale(self) -> float:
+        """Factor that turns the summed gradient into the mean over ranks."""
+        return 1.0 / self.world
+
+
+def shard_len(n: int, world: int, align: int = 16) -> int:
+    """Per-rank shard length of an n-element flat bucket: buckets are padded to
+    world * shard elements, shards are multiples of ``align`` elements (16
+    elements keep every shard 32-byte aligned for bf16 and fp32 vectors)."""
+    per = -(-n // world)
+    return -(-per // align) * align
+
+
+class ShardedBucketOptimizer:
+    """ZeRO-1 over flat buckets (see the module docstring).
+
+    ``sizes`` maps a bucket key to its element count.  Gradient and parameter
+    buckets handed in must have ``padded_len(key)`` elements (the tail past
+    the real size is padding that stays zero in the gradient).  ``update_fn(p,
+    g, m, v)`` updates one shard in place: p is this rank's slice of the
+    parameter bucket, g the reduce-scattered gradient sum, m/v the shard's
+    optimizer state (fp32, zero-initialised)."""
+
+    def __init__(self, process_group, sizes: Dict[Hashable, int], device, grad_dtype=torch.bfloat16):
+        self.pg = process_group
+        self.world = dist.get_world_size(process_group)
+        self.rank = dist.get_rank(process_group)
+        self.shard = {k: shard_len(n, self.world) for k, n in sizes.items()}
+        self.grad_shard = {k: torch.zeros(s, device=device, dtype=grad_dtype) for k, s in self.shard.items()}
+        self.m = {k: torch.zeros(s, device=device, dtype=torch.float32) for k, s in self.shard.items()}
+        self.v = {k: torch.zeros(s, device=device, dtype=torch.float32) for k, s in self.shard.items()}
+        self.rs_works: Dict[Hashable, object] = {}
+        self.ag_works: Dict[Hashable, object] = {}
+
+    def padded_len(self, key: Hashable) -> int:
+        return self.shard[key] * self.world
+
+    def shard_slice(self, key: Hashable) -> slice:
+        s = self.shard[key]
+        return slice(self.rank * s, (self.rank + 1) * s)
+
+    def reduce_scatter(self, key: Hashable, grad_full: torch.Tensor) -> None:
+        if grad_full.numel() != self.padded_len(key):
+            raise RuntimeError(f"bucket {key!r}: gradient has {grad_full.numel()} elements, "
+                               f"expected the padded length {self.padded_len(key)}")
+        if key in self.rs_works:
+            raise RuntimeError(f"bucket {key!r} already in flight")
+        self.rs_works[key] = dist.reduce_scatter_tensor(self.grad_shard[key], grad_full, op=dist.ReduceOp.SUM,
+                                                        group=self.pg, async_op=True)
+
+    def update(self, key: Hashable, param_full: torch.Tensor, update_fn, timeout_s: Optional[float] = None,
+               gather: bool = True) -> None:
+        """Wait for the bucket's reduce-scatter and update this rank's shard;
+        with ``gather`` also start the all-gather of the updated parameters
+        (otherwise call ``gather`` later, e.g. in the order the next forward
+        needs the buckets)."""
+        w = self.rs_works.pop(key, None)
+        if w is None:
+            raise RuntimeError(f"bucket {key!r}: no reduce-scatter in flight")
+        if timeout_s is None:
+            w.wait()
+        else:
+            w.wait(timeout=datetime.timedelta(seconds=timeout_s))
+        if param_full.numel() != self.padded_len(key):
+            raise RuntimeError(f"bucket {key!r}: parameters have {param_full.numel()} elements, "
+                               f"expected the padded length {self.padded_len(key)}")
+        p_shard = param_full[self.shard_slice(key)]
+        update_fn(p_shard, self.grad_shard[key], self.m[key], self.v[key])
+        if gather:
+            self.gather(key, param_full)
+
+    def gather(self, key: Hashable, param_full: torch.Tensor) -> None:
+        """Start the all-gather of every rank's updated shard into ``param_full``."""
+        if key in self.ag_works:
+            raise RuntimeError(f"bucket {key!r}: gather already in flight")
+        p_shard = param_full[self.shard_slice(key)]
+        self.ag_works[key] = dist.all_gather_into_tensor(param_full, p_shard, group=self.pg, async_op=True)
+
+    def wait_params(self, key: Hashable, timeout_s: Optional[float] = None) -> None:
+        """Make the current stream wait until the bucket's gathered parameters are in place."""
+        w = self.ag_works.pop(key, None)
+        if w is None:
+            return
+        if timeout_s is None:
+            w.wait()
+        else:
+            w.wait(timeout=datetime.timedelta(seconds=timeout_s))
+
+    def wait_all(self) -> None:
+        for k in list(self.ag_works):
+            self.wait_params(k)
 
     def grad_scale(self) -> float:
         """Factor that turns the summed gradient into the mean over ranks."""

@@ -33,7 +33,7 @@ import torch
 import torch.nn as nn
 
 from . import ops
-from .dp import BucketAllReducer
+from .dp import BucketAllReducer, ShardedBucketOptimizer
 
 
 @dataclass
@@ -180,14 +180,19 @@ class AdamConfig:
 
 
 class BlockState:
-    """Flat bf16 parameter / gradient buckets and fp32 Adam moments of one block."""
+    """Flat bf16 parameter / gradient buckets and fp32 Adam moments of one block.
+
+    ``pad_to`` (>= the real size) pads both buckets with zeros so that a
+    reduce-scatter divides them evenly; ``with_moments=False`` leaves the Adam
+    moments to a sharded optimizer."""
 
     def __init__(self, d: int, f: int, device, gen: Optional[torch.Generator], init_std: float,
-                 grad_f32: bool):
+                 grad_f32: bool, pad_to: int = 0, with_moments: bool = True):
         self.d, self.f = d, f
         n = d + 2 * f * d + d * f
         self.numel = n
-        self.param = torch.empty(n, device=device, dtype=torch.bfloat16)
+        length = max(n, pad_to)
+        self.param = torch.zeros(length, device=device, dtype=torch.bfloat16)
         self.gamma = self.param[:d]
         self.w_gu = self.param[d:d + 2 * f * d].view(2 * f, d)
         self.w_down = self.param[d + 2 * f * d:].view(d, f)
@@ -195,10 +200,10 @@ class BlockState:
             self.gamma.fill_(1.0)
             w = torch.empty(2 * f * d + d * f, device=device, dtype=torch.float32)
             w.normal_(0.0, init_std, generator=gen)
-            self.param[d:].copy_(w)
+            self.param[d:n].copy_(w)
             del w
-        # bf16 gradient bucket (the all-reduce payload): gamma | W_gu | W_down
-        self.grad = torch.zeros(n, device=device, dtype=torch.bfloat16)
+        # bf16 gradient bucket (the all-reduce / reduce-scatter payload): gamma | W_gu | W_down | padding
+        self.grad = torch.zeros(length, device=device, dtype=torch.bfloat16)
         self.grad_gamma32 = torch.zeros(d, device=device, dtype=torch.float32)
         self.grad_gu = self.grad[d:d + 2 * f * d].view(2 * f, d)
         self.grad_down = self.grad[d + 2 * f * d:].view(d, f)
@@ -207,22 +212,30 @@ class BlockState:
             self.acc_down = torch.zeros(d, f, device=device, dtype=torch.float32)
         else:
             self.acc_gu = self.acc_down = None
-        self.m = torch.zeros(n, device=device, dtype=torch.float32)
-        self.v = torch.zeros(n, device=device, dtype=torch.float32)
+        self.m = torch.zeros(length, device=device, dtype=torch.float32) if with_moments else None
+        self.v = torch.zeros(length, device=device, dtype=torch.float32) if with_moments else None
 
 
 class NVFP4MLPStackTrainer:
     """Training step of a stack of NVFP4 RMSNorm+SwiGLU blocks.
 
     One step: forward over all blocks (micro-batched), backward from a given
-    upstream gradient, per-block bf16 gradient all-reduce (NCCL through
-    torch.distributed when a process group is initialised) launched as soon
-    as the block's wgrads are done so it overlaps the backward of the blocks
-    below, then the fp32 AdamW update of every block."""
+    upstream gradient, then the fp32 AdamW update.  With a process group of
+    more than one rank the per-block bf16 gradient bucket is exchanged as soon
+    as the block's wgrads are done, overlapping the backward of the blocks
+    below:
+
+    * ``zero=True`` (default): reduce-scatter, AdamW of this rank's shard, and
+      an all-gather of the updated parameters that the next step waits for
+      just before quantizing that block's weights;
+    * ``zero=False``: all-reduce and AdamW of the whole block on every rank.
+
+    ``finish()`` waits for parameter gathers still in flight."""
 
     def __init__(self, n_blocks: int, d_model: int, d_ff: int, *, device="cuda", seed: int = 0,
                  micro_tokens: int = 16384, eps: float = 1e-6, adam: Optional[AdamConfig] = None,
-                 init_std: float = 0.02, process_group=None, max_local_tokens: Optional[int] = None):
+                 init_std: float = 0.02, process_group=None, max_local_tokens: Optional[int] = None,
+                 comm_sms: int = 0, zero: bool = True):
         self.device = torch.device(device)
         self.n_blocks, self.d, self.f = n_blocks, d_model, d_ff
         self.micro_tokens = micro_tokens
@@ -231,18 +244,52 @@ class NVFP4MLPStackTrainer:
         self.pg = process_group
         gen = torch.Generator(device=self.device).manual_seed(seed)
         grad_f32 = max_local_tokens is None or max_local_tokens > micro_tokens
-        self.blocks = [BlockState(d_model, d_ff, self.device, gen, init_std, grad_f32) for _ in range(n_blocks)]
+        world = 1
+        if process_group is not None:
+            import torch.distributed as dist
+            world = dist.get_world_size(process_group)
+        self.world = world
+        n = d_model + 3 * d_ff * d_model
+        self.opt = None
+        self.reducer = None
+        if world > 1 and zero:
+            self.opt = ShardedBucketOptimizer(process_group, {i: n for i in range(n_blocks)}, self.device)
+            self.blocks = [BlockState(d_model, d_ff, self.device, gen, init_std, grad_f32,
+                                      pad_to=self.opt.padded_len(i), with_moments=False) for i in range(n_blocks)]
+        else:
+            self.blocks = [BlockState(d_model, d_ff, self.device, gen, init_std, grad_f32) for _ in range(n_blocks)]
+            if world > 1:
+                self.reducer = BucketAllReducer(process_group)
         self.step_count = 0
-        self.reducer = BucketAllReducer(process_group) if process_group is not None else None
-        self.world = self.reducer.world if self.reducer is not None else 1
+        # SMs left to the gradient collectives while the step's GEMMs run (DP only)
+        self.comm_sms = comm_sms if world > 1 else 0
+        self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
 
     # -- one optimizer step -------------------------------------------------
     def step(self, x: torch.Tensor, dy: torch.Tensor) -> torch.Tensor:
         """x, dy: bf16 [T_local, D] on this rank's device.  Returns a 1-element
         fp32 tensor (sum of the output, a cheap device-side step result)."""
+        if self.comm_sms > 0:
+            ops.set_gemm_max_sms(max(2, self.sm_count - self.comm_sms))
+        try:
+            return self._step(x, dy)
+        finally:
+            if self.comm_sms > 0:
+                ops.set_gemm_max_sms(0)
+
+    def _step(self, x: torch.Tensor, dy: torch.Tensor) -> torch.Tensor:
         t = x.shape[0]
         n_micro = max(1, math.ceil(t / self.micro_tokens))
-        qws = [quantize_weights(b.w_gu, b.w_down, need_t=True) for b in self.blocks]
+        qws: List[Optional[QWeights]] = [None] * self.n_blocks
+
+        def qw(bi: int) -> QWeights:   # quantize a block's weights on first use (after its gather landed)
+            if qws[bi] is None:
+                if self.opt is not None:
+                    self.opt.wait_params(bi)
+                b = self.blocks[bi]
+                qws[bi] = quantize_weights(b.w_gu, b.w_down, need_t=True)
+            return qws[bi]
+
         for b in self.blocks:
             b.grad_gamma32.zero_()
         out_sum = torch.zeros(1, device=self.device, dtype=torch.float32)
@@ -251,7 +298,7 @@ class NVFP4MLPStackTrainer:
             h = x[lo:hi]
             saved: List[Saved] = []
             for bi, b in enumerate(self.blocks):
-                h, sv = block_forward(h, b.gamma, qws[bi], self.eps)
+                h, sv = block_forward(h, b.gamma, qw(bi), self.eps)
                 saved.append(sv)
             out_sum += h.sum(dtype=torch.float32)
             g = dy[lo:hi]
@@ -271,16 +318,36 @@ class NVFP4MLPStackTrainer:
                 saved[bi] = None
                 if last:
                     b.grad[:self.d].copy_(b.grad_gamma32)
-                    if self.reducer is not None:
+                    if self.opt is not None:
+                        self.opt.reduce_scatter(bi, b.grad)
+                    elif self.reducer is not None:
                         self.reducer.launch(bi, b.grad)
         self.step_count += 1
         a = self.adam
-        for bi, b in enumerate(self.blocks):
-            if self.reducer is not None:
-                self.reducer.wait(bi)
-            ops.adamw_step(b.param, b.grad, b.m, b.v, lr=a.lr, beta1=a.beta1, beta2=a.beta2, eps=a.eps,
+
+        def adamw(p, g, m, v):
+            ops.adamw_step(p, g, m, v, lr=a.lr, beta1=a.beta1, beta2=a.beta2, eps=a.eps,
                            weight_decay=a.weight_decay, step=self.step_count, grad_scale=1.0 / self.world)
+
+        # buckets were launched from the last block down: update in that order
+        for bi in reversed(range(self.n_blocks)):
+            b = self.blocks[bi]
+            if self.opt is not None:
+                self.opt.update(bi, b.param, adamw, gather=False)
+            else:
+                if self.reducer is not None:
+                    self.reducer.wait(bi)
+                adamw(b.param, b.grad, b.m, b.v)
+        if self.opt is not None:
+            # gathers in the order the next forward uses the blocks: block 0 lands first
+            for bi, b in enumerate(self.blocks):
+                self.opt.gather(bi, b.param)
         return out_sum
+
+    def finish(self) -> None:
+        """Make the current stream wait for every parameter gather still in flight."""
+        if self.opt is not None:
+            self.opt.wait_all()
 
     def flops_per_step(self, tokens: int) -> float:
         return 3 * 3 * 2.0 * tokens * self.d * self.f * self.n_blocks

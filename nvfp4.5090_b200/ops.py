@@ -172,6 +172,12 @@ def global_scale(x: torch.Tensor, with_amax: bool = False):
 # ----------------------------------------------------------------------------
 
 
+def set_gemm_max_sms(max_sms: int) -> None:
+    """Cap the SMs a GEMM launch occupies (0 = all).  Process-wide; a
+    data-parallel step lowers it so NCCL kernels run beside the GEMMs."""
+    _lib.call("nvfp4b200_set_gemm_max_sms", int(max_sms))
+
+
 def gemm(qa: torch.Tensor, sa: torch.Tensor, qb: torch.Tensor, sb: torch.Tensor, *,
          scale_a: Optional[torch.Tensor] = None, scale_b: Optional[torch.Tensor] = None,
          bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,

@@ -1,6 +1,8 @@
 """Data-parallel host logic on CPU with world_size-2 gloo process groups:
-bucketed async all-reduce, mean-gradient scaling, and host-side failure
-detection (a rank that dies before the collective)."""
+bucketed async all-reduce, mean-gradient scaling, the ZeRO-1 sharded
+optimizer (reduce-scatter, shard update, all-gather) against the all-reduce
+path, and host-side failure detection (a rank that dies before the
+collective)."""
 import datetime
 import os
 import socket
@@ -62,6 +64,70 @@ def _worker_reduce(rank, world, port, q):
         q.put((rank, traceback.format_exc()))
 
 
+def _adam_cpu(p, g, m, v, step=1, lr=1e-2, b1=0.9, b2=0.95, eps=1e-8, gscale=0.5):
+    """Elementwise AdamW-like update on CPU tensors (p bf16, g bf16, m/v fp32), in place."""
+    gf = g.float() * gscale
+    m.mul_(b1).add_((1 - b1) * gf)
+    v.mul_(b2).add_((1 - b2) * gf * gf)
+    upd = (m / (1 - b1 ** step)) / ((v / (1 - b2 ** step)).sqrt() + eps)
+    p.copy_((p.float() - lr * upd).to(p.dtype))
+
+
+def _worker_sharded(rank, world, port, q):
+    try:
+        _init(rank, world, port, 30)
+        dp = _dp_module()
+        sizes = {0: 1001, 1: 37, 2: 4096}
+        opt = dp.ShardedBucketOptimizer(dist.group.WORLD, sizes, "cpu")
+        assert opt.world == world and opt.grad_scale() == 1.0 / world
+        gen = torch.Generator().manual_seed(0)            # same initial parameters on every rank
+        params = {k: torch.zeros(opt.padded_len(k), dtype=torch.bfloat16) for k in sizes}
+        for k, n in sizes.items():
+            params[k][:n] = torch.randn(n, generator=gen).to(torch.bfloat16)
+        ref = {k: p.clone() for k, p in params.items()}
+        ref_m = {k: torch.zeros(opt.padded_len(k)) for k in sizes}
+        ref_v = {k: torch.zeros(opt.padded_len(k)) for k in sizes}
+        for step in (1, 2):
+            grads = {}
+            for k, n in sizes.items():                   # rank-dependent gradients, zero padding
+                gk = torch.zeros(opt.padded_len(k), dtype=torch.bfloat16)
+                gk[:n] = (torch.arange(n, dtype=torch.float32) * 0.01 * (rank + 1) + step).to(torch.bfloat16)
+                grads[k] = gk
+            # reference: all-reduce the full bucket, update the full bucket
+            for k in sizes:
+                g_all = grads[k].clone()
+                dist.all_reduce(g_all)
+                _adam_cpu(ref[k], g_all, ref_m[k], ref_v[k], step=step)
+            # sharded: reduce-scatter, shard update, all-gather (launched last block first)
+            for k in reversed(list(sizes)):
+                opt.reduce_scatter(k, grads[k])
+            for k in reversed(list(sizes)):
+                opt.update(k, params[k], lambda p, g, m, v: _adam_cpu(p, g, m, v, step=step))
+            opt.wait_all()
+            for k, n in sizes.items():
+                assert torch.equal(params[k], ref[k]), (k, step)
+                assert torch.all(params[k][n:] == 0)     # padding stays zero
+        bad = torch.zeros(7, dtype=torch.bfloat16)
+        try:
+            opt.reduce_scatter(0, bad)
+            raise AssertionError("wrong-length bucket accepted")
+        except RuntimeError:
+            pass
+        opt.reduce_scatter(1, torch.zeros(opt.padded_len(1), dtype=torch.bfloat16))
+        try:
+            opt.reduce_scatter(1, torch.zeros(opt.padded_len(1), dtype=torch.bfloat16))
+            raise AssertionError("second reduce-scatter of a bucket in flight accepted")
+        except RuntimeError:
+            pass
+        opt.update(1, params[1], lambda p, g, m, v: None)
+        opt.wait_all()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
 def _worker_failure(rank, world, port, q):
     try:
         _init(rank, world, port, 4)
@@ -104,6 +170,19 @@ def _run(target, world=2, timeout=60):
 def test_bucketed_allreduce_two_ranks():
     out = _run(_worker_reduce)
     assert out == {0: "ok", 1: "ok"}, out
+
+
+def test_sharded_optimizer_matches_allreduce_two_ranks():
+    out = _run(_worker_sharded)
+    assert out == {0: "ok", 1: "ok"}, out
+
+
+def test_shard_len_pads_evenly():
+    dp = _dp_module()
+    for n in (1, 15, 16, 1001, 4096, 123457):
+        for world in (1, 2, 3, 8):
+            s = dp.shard_len(n, world)
+            assert s % 16 == 0 and s * world >= n and (s - 16) * world < n
 
 
 def test_rank_failure_is_detected_on_host():
