@@ -59,7 +59,33 @@ __device__ __forceinline__ float e4m3_decode(uint32_t c) {
                 : __uint_as_float(((e + 120u) << 23) | (m << 20));
 }
 
-// Pack 8 floats into 8 E2M1 nibbles (low nibble = even element,
+// ---------------------------------------------------------------------------
+// packed f32 pairs: one 64-bit register holds two floats and each f32x2
+// instruction performs two independent IEEE single-precision operations,
+// with the same results as two scalar ones (round to nearest, no flush).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float f2lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t f2mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// a * b + (+0, +0), one rounding per lane
+__device__ __forceinline__ uint64_t f2mul_plus_zero(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(0ull));
+  return r;
+}
+// bf16 pair word -> {lo, hi} as a packed f32 pair, exactly
+__device__ __forceinline__ uint64_t bf16x2_to_f2(uint32_t w) { return f2pack(bf16lo(w), bf16hi(w)); }
+
+// encode8_pairs: 8 values (4 packed pairs) -> 8 E2M1 nibbles (low nibble = even element,
 // float4utils.py:141), each nibble equal to the reference's comparison ladder
 // (float4utils.py:127-139): magnitude code = #{t in {0.25,0.75,1.25,1.75,
 // 2.5,3.5,5} : !(|f * inv_scale| < t)} after clamping to 6 (ties round away
@@ -78,23 +104,17 @@ __device__ __forceinline__ float e4m3_decode(uint32_t c) {
 //     -FLT_MAX, which saturates to -6 like the ladder; arithmetic NaN results
 //     are the positive canonical NaN, which the instruction turns into +6.
 // An exhaustive GPU sweep over every f32 bit pattern checks this identity.
-__device__ __forceinline__ float fma_plus_zero(float a, float b) {
-  float r;
-  asm("fma.rn.f32 %0, %1, %2, 0f00000000;" : "=f"(r) : "f"(a), "f"(b));
-  return r;
-}
-// CLAMP = false skips the -inf adjustment; valid whenever the block amax is
-// finite (then no product is -inf).
 template <bool CLAMP = true>
-__device__ __forceinline__ float e2m1_input(float f, float inv_scale) {
-  const uint32_t b = __float_as_uint(fma_plus_zero(f, inv_scale));
-  return __uint_as_float((CLAMP ? min(b, 0xFF7FFFFFu) : b) | 1u);
-}
-template <bool CLAMP = true>
-__device__ __forceinline__ uint32_t encode8(const float* f, float inv_scale) {
+__device__ __forceinline__ uint32_t encode8_pairs(const uint64_t* p, float inv_scale) {
+  const uint64_t is2 = f2pack(inv_scale, inv_scale);
   float q[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) q[i] = e2m1_input<CLAMP>(f[i], inv_scale);
+  for (int j = 0; j < 4; ++j) {
+    const uint64_t r = f2mul_plus_zero(p[j], is2);
+    const uint32_t lo = __float_as_uint(f2lo(r)), hi = __float_as_uint(f2hi(r));
+    q[2 * j] = __uint_as_float((CLAMP ? min(lo, 0xFF7FFFFFu) : lo) | 1u);
+    q[2 * j + 1] = __uint_as_float((CLAMP ? min(hi, 0xFF7FFFFFu) : hi) | 1u);
+  }
   uint32_t out;
   asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
       "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
@@ -106,28 +126,54 @@ __device__ __forceinline__ uint32_t encode8(const float* f, float inv_scale) {
       : "f"(q[0]), "f"(q[1]), "f"(q[2]), "f"(q[3]), "f"(q[4]), "f"(q[5]), "f"(q[6]), "f"(q[7]));
   return out;
 }
-
-// Block scale from a block amax (float4utils.py:109-116 with the global scale
-// g folded in; g == 1 is bit-identical to the reference):
-//   code      = e4m3_satfinite((amax * (1/6)) * inv_g)        (0 when amax == 0)
-//   inv_scale = code decodes to s > 0 ? 1 / (s * g) : 1
-__device__ __forceinline__ uint32_t block_scale(float amax, float g, float inv_g, float& inv_scale) {
-  uint32_t code = 0;
-  inv_scale = 1.0f;
-  if (amax > 0.0f) {
-    const float scale_f = (amax * (1.0f / 6.0f)) * inv_g;
-    code = e4m3_rn_satfinite(scale_f);
-    const float s = e4m3_decode(code);
-    inv_scale = (s > 0.0f) ? __frcp_rn(s * g) : 1.0f;
+// 8 packed pairs (one block) -> 8 bytes of nibbles; -inf adjustment only for an infinite amax.
+__device__ __forceinline__ uint2 encode16_pairs(const uint64_t (&p)[8], float inv_scale, float amax) {
+  if (amax <= 3.402823466e38f) return make_uint2(encode8_pairs<false>(p, inv_scale), encode8_pairs<false>(p + 4, inv_scale));
+  return make_uint2(encode8_pairs<true>(p, inv_scale), encode8_pairs<true>(p + 4, inv_scale));
+}
+// Two output rows at once: p[t] = {row a value t, row b value t} for t < 16
+// (a block of each row).  Returns the nibbles of row a (x) and row b (y)
+// with per-row inverse scales; the -inf adjustment only when a block amax is
+// infinite.
+__device__ __forceinline__ void encode16_two_rows(const uint64_t (&p)[16], float inv_a, float inv_b, float amax_a,
+                                                  float amax_b, uint2& out_a, uint2& out_b) {
+  const uint64_t is2 = f2pack(inv_a, inv_b);
+  const bool clamp = !(amax_a <= 3.402823466e38f) || !(amax_b <= 3.402823466e38f);
+  float qa[16], qb[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    const uint64_t r = f2mul_plus_zero(p[t], is2);
+    uint32_t lo = (uint32_t)r, hi = (uint32_t)(r >> 32);
+    if (clamp) {
+      lo = min(lo, 0xFF7FFFFFu);
+      hi = min(hi, 0xFF7FFFFFu);
+    }
+    qa[t] = __uint_as_float(lo | 1u);
+    qb[t] = __uint_as_float(hi | 1u);
   }
-  return code;
+  uint32_t w[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const float* q = h < 2 ? qa + 8 * h : qb + 8 * (h - 2);
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+        "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+        : "=r"(w[h])
+        : "f"(q[0]), "f"(q[1]), "f"(q[2]), "f"(q[3]), "f"(q[4]), "f"(q[5]), "f"(q[6]), "f"(q[7]));
+  }
+  out_a = make_uint2(w[0], w[1]);
+  out_b = make_uint2(w[2], w[3]);
 }
 
-// 16 floats (one block) -> 8 bytes of nibbles, the -inf adjustment only when
-// the block amax is infinite.
-__device__ __forceinline__ uint2 encode16(const float (&f)[16], float inv_scale, float amax) {
-  if (amax <= 3.402823466e38f) return make_uint2(encode8<false>(f, inv_scale), encode8<false>(f + 8, inv_scale));
-  return make_uint2(encode8<true>(f, inv_scale), encode8<true>(f + 8, inv_scale));
+// fmaxf-semantics amax over 8 packed pairs (NaN dropped).
+__device__ __forceinline__ float fmax_abs16_pairs(const uint64_t (&p)[8]) {
+  float a = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) a = fmaxf(a, fmaxf(fabsf(f2lo(p[j])), fabsf(f2hi(p[j]))));
+  return a;
 }
 
 // E4M3 block-scale code of a block amax (float4utils.py:109-116 with the
@@ -138,8 +184,8 @@ __device__ __forceinline__ uint32_t block_code(float amax, float inv_g) {
 }
 
 // Table of inv_scale for every block-scale code under global scale g:
-// 1 / (decode(c) * g) rounded once (the value block_scale computes), 1 for a
-// zero scale.  Filled by the CTA's threads before first use.
+// 1 / (decode(c) * g) rounded once (float4utils.py:114-116 with g folded in), 1
+// for a zero scale.  Filled by the CTA's threads before first use.
 __device__ __forceinline__ void fill_inv_scale_table(float* tab, float g) {
   for (int c = threadIdx.x; c < 256; c += blockDim.x) {
     const float sv = e4m3_decode((uint32_t)c & 0x7Fu);
@@ -154,31 +200,6 @@ __device__ __forceinline__ uint32_t absmax16_bits(const uint32_t (&w)[8]) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) m = __vmaxu2(m, w[i] & 0x7FFF7FFFu);
   return max(m & 0xFFFFu, m >> 16);
-}
-
-// fmaxf-semantics amax over 16 floats (NaN dropped).
-__device__ __forceinline__ float fmax_abs16(const float (&f)[16]) {
-  float a = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) a = fmaxf(a, fabsf(f[i]));
-  return a;
-}
-
-// Block amax of 8 bf16 values held as 4 words: integer max of |x| bit
-// patterns (positive bf16 order like integers).  Returns the 16-bit pattern.
-__device__ __forceinline__ uint32_t absmax8_bits(const uint32_t (&w)[4]) {
-  uint32_t m = __vmaxu2(__vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
-                        __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
-  return max(m & 0xFFFFu, m >> 16);
-}
-
-// fmaxf-semantics amax (NaN dropped) over floats, used on the rare blocks
-// whose integer max is a NaN pattern.
-__device__ __forceinline__ float fmax_abs8(const float (&f)[8]) {
-  float a = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(f[i]));
-  return a;
 }
 
 // Swizzled scale byte offset (float4utils.py:118-122): atom (r/128, c/4) of

@@ -84,28 +84,23 @@ __global__ void __launch_bounds__(256) global_amax_kernel(const uint4* __restric
 // tile quantizer: 128 rows x 512 columns per CTA
 // ---------------------------------------------------------------------------
 // Each lane owns one 16-element block column of the tile (32 B of every row);
-// a warp covers 16 rows, read 4 rows per pass with the next pass's loads in
-// flight while the current one is encoded.  Per row a warp reads 1 KB and
+// a warp covers 16 rows, read a few rows per pass (2 for the plain quantizer,
+// 4 with row scale or gamma: measured best for each) with the next pass's
+// loads in flight while the current one is encoded.  Per row a warp reads 1 KB and
 // writes 256 B of nibbles; the tile's 8 scale atoms (4 KB, contiguous in the
 // swizzled layout) are staged in shared memory and written whole.
 
 constexpr int QT_ROWS = 128;
 constexpr int QT_COLS = 512;       // 32 blocks = 8 scale atoms
 constexpr int QT_THREADS = 256;    // 8 warps x 16 rows
-constexpr int QT_PASS = 4;         // rows per pipelined pass
 
-__device__ __forceinline__ void unpack16(const uint4 a, const uint4 b, uint32_t (&w)[8], float (&f)[16]) {
-  w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
-  w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) { f[2 * i] = bf16lo(w[i]); f[2 * i + 1] = bf16hi(w[i]); }
-}
 
 template <bool HAS_ROW, bool HAS_GAMMA>
 __global__ void __launch_bounds__(QT_THREADS) quant_tile_kernel(
     const uint16_t* __restrict__ x, const float* __restrict__ row_scale,
     const uint16_t* __restrict__ gamma, uint8_t* __restrict__ q, uint8_t* __restrict__ s,
     int64_t rows, int64_t k, int64_t pad_cols, const float* __restrict__ gptr, int q8) {
+  constexpr int QT_PASS = (HAS_ROW || HAS_GAMMA) ? 4 : 2;  // rows per pipelined pass
   __shared__ __align__(16) uint8_t s_tile[8 * 512];
   __shared__ float inv_tab[256];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -116,15 +111,16 @@ __global__ void __launch_bounds__(QT_THREADS) quant_tile_kernel(
   const float inv_g = __frcp_rn(g);
   fill_inv_scale_table(inv_tab, g);
 
-  float gam[16];
+  uint64_t gam[8];   // gamma as packed pairs
   if (HAS_GAMMA) {
     uint4 ga = make_uint4(0, 0, 0, 0), gb = ga;
     if (col_ok) {
       ga = __ldg(reinterpret_cast<const uint4*>(gamma + col));
       gb = __ldg(reinterpret_cast<const uint4*>(gamma + col) + 1);
     }
-    uint32_t gw[8];
-    unpack16(ga, gb, gw, gam);
+    const uint32_t gw[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) gam[j] = bf16x2_to_f2(gw[j]);
   }
   __syncthreads();  // inv_tab
 
@@ -151,24 +147,27 @@ __global__ void __launch_bounds__(QT_THREADS) quant_tile_kernel(
       const int rl = wid * 16 + pass * QT_PASS + i;  // row inside the tile
       const int64_t r = tile_r0 + rl;
       const bool ok = col_ok && r < rows;
-      uint32_t w[8];
-      float f[16];
-      unpack16(cur[i][0], cur[i][1], w, f);
+      const uint32_t w[8] = {cur[i][0].x, cur[i][0].y, cur[i][0].z, cur[i][0].w,
+                             cur[i][1].x, cur[i][1].y, cur[i][1].z, cur[i][1].w};
+      uint64_t f[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = bf16x2_to_f2(w[j]);
       float amax;
       if (HAS_ROW || HAS_GAMMA) {
         const float rs = HAS_ROW ? (r < rows ? __ldg(row_scale + r) : 0.0f) : 1.0f;
+        const uint64_t rs2 = f2pack(rs, rs);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (HAS_ROW) f[j] = f[j] * rs;
-          if (HAS_GAMMA) f[j] = f[j] * gam[j];
+        for (int j = 0; j < 8; ++j) {
+          if (HAS_ROW) f[j] = f2mul(f[j], rs2);
+          if (HAS_GAMMA) f[j] = f2mul(f[j], gam[j]);
         }
-        amax = fmax_abs16(f);
+        amax = fmax_abs16_pairs(f);
       } else {
         const uint32_t mb = absmax16_bits(w);
-        amax = (mb > 0x7F80u) ? fmax_abs16(f) : __uint_as_float(mb << 16);
+        amax = (mb > 0x7F80u) ? fmax_abs16_pairs(f) : __uint_as_float(mb << 16);
       }
       const uint32_t code = ok ? block_code(amax, inv_g) : 0u;
-      const uint2 packed = encode16(f, inv_tab[code], amax);
+      const uint2 packed = encode16_pairs(f, inv_tab[code], amax);
       if (ok) {
         uint8_t* dst = q + r * (k >> 1) + (col >> 1);
         if (q8) {
@@ -296,7 +295,7 @@ __global__ void __launch_bounds__(256) rmsnorm_cta_kernel(
     inv_g = __frcp_rn(g);
     fill_inv_scale_table(inv_tab, g);
   }
-  float gam[BPT][16];
+  uint64_t gam[BPT][8];   // gamma as packed pairs
   if (HAS_GAMMA) {
 #pragma unroll
     for (int b = 0; b < BPT; ++b) {
@@ -307,8 +306,9 @@ __global__ void __launch_bounds__(256) rmsnorm_cta_kernel(
         g0 = __ldg(gp);
         g1 = __ldg(gp + 1);
       }
-      uint32_t gw[8];
-      unpack16(g0, g1, gw, gam[b]);
+      const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) gam[b][j] = bf16x2_to_f2(gw[j]);
     }
   }
   auto load_row = [&](int64_t r, uint4 (&buf)[BPT][2]) {
@@ -336,47 +336,57 @@ __global__ void __launch_bounds__(256) rmsnorm_cta_kernel(
         *reinterpret_cast<uint32_t*>(s + swz_offset(r, c, pad_cols)) = 0u;
       continue;
     }
-    float f[BPT][16];
+    uint64_t f[BPT][8];
     float ss = 0.0f;
 #pragma unroll
     for (int b = 0; b < BPT; ++b) {
-      uint32_t w[8];
-      unpack16(cur[b][0], cur[b][1], w, f[b]);
-      if (t + 256 * b < nblk) ss = sumsq_block(ss, cur[b][0], cur[b][1]);
+      const uint32_t w[8] = {cur[b][0].x, cur[b][0].y, cur[b][0].z, cur[b][0].w,
+                             cur[b][1].x, cur[b][1].y, cur[b][1].z, cur[b][1].w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[b][j] = bf16x2_to_f2(w[j]);
+      if (t + 256 * b < nblk) {
+        // ``ss += a0 * a0 + a1 * a1`` (the squares of bf16 values are exact in fp32, so
+        // the packed product gives the reference's terms bit for bit)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint64_t sq = f2mul(f[b][j], f[b][j]);
+          ss += f2lo(sq) + f2hi(sq);
+        }
+      }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_down_sync(0xffffffffu, ss, off);
     if (lane == 0) warp_sum[wid] = ss;
     __syncthreads();
-    if (wid == 0) {
+    if (wid == 0) {   // the reference's final tree over the warp sums
       float v = (lane < nwarps) ? warp_sum[lane] : 0.0f;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) v += __shfl_down_sync(0xffffffffu, v, off);
       if (lane == 0) {
-        const float inv = rsqrtf((v / (float)k) + eps);
-        row_inv = inv;
-        if (inv_rms_out) inv_rms_out[r] = inv;
+        const float iv = rsqrtf((v / (float)k) + eps);
+        row_inv = iv;
+        if (inv_rms_out) inv_rms_out[r] = iv;
       }
     }
     __syncthreads();
     const float inv = row_inv;
+    const uint64_t inv2 = f2pack(inv, inv);
 #pragma unroll
     for (int b = 0; b < BPT; ++b) {
       const int64_t c = t + 256 * b;
       const bool in = c < nblk;
 #pragma unroll
-      for (int e = 0; e < 16; ++e) f[b][e] = f[b][e] * inv;
-      if (HAS_GAMMA) {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) f[b][e] = f[b][e] * gam[b][e];
+      for (int j = 0; j < 8; ++j) {
+        f[b][j] = f2mul(f[b][j], inv2);
+        if (HAS_GAMMA) f[b][j] = f2mul(f[b][j], gam[b][j]);
       }
-      const float amax = in ? fmax_abs16(f[b]) : 0.0f;
+      const float amax = in ? fmax_abs16_pairs(f[b]) : 0.0f;
       if (MODE == 1) {
         am = fmaxf(am, amax);
         continue;
       }
       const uint32_t code = in ? block_code(amax, inv_g) : 0u;
-      const uint2 packed = encode16(f[b], inv_tab[code], amax);
+      const uint2 packed = encode16_pairs(f[b], inv_tab[code], amax);
       if (in) {
         uint8_t* dst = q + r * (k >> 1) + 8 * c;
         if (q8) {
@@ -508,35 +518,31 @@ __global__ void __launch_bounds__(256) quant_t_kernel(
       if (d0 + dl0 < cols) gam0 = __uint_as_float((uint32_t)gamma[d0 + dl0] << 16);
       if (d0 + dl0 + 1 < cols) gam1 = __uint_as_float((uint32_t)gamma[d0 + dl0 + 1] << 16);
     }
+    const uint64_t gam2 = f2pack(gam0, gam1);
     uint32_t qwa[4], qwb[4];
     uint32_t codes_a = 0, codes_b = 0;
 #pragma unroll
     for (int bi = 0; bi < 2; ++bi) {
       const int b = 2 * qtr + bi;
-      float fa[16], fb[16];
+      uint64_t pr[16];   // {output row dl0, output row dl0 + 1} at input row t
+      float ama = 0.0f, amb = 0.0f;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int t = b * 16 + j;
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(tl + t * TQ_D + dl0);
-        float a = bf16lo(w), c = bf16hi(w);
+        pr[j] = bf16x2_to_f2(*reinterpret_cast<const uint32_t*>(tl + t * TQ_D + dl0));
         if (HAS_ROW) {
           const float rsv = sm.rs[buf][t];
-          a = a * rsv;
-          c = c * rsv;
+          pr[j] = f2mul(pr[j], f2pack(rsv, rsv));
         }
-        if (HAS_GAMMA) {
-          a = a * gam0;
-          c = c * gam1;
-        }
-        fa[j] = a;
-        fb[j] = c;
+        if (HAS_GAMMA) pr[j] = f2mul(pr[j], gam2);
+        ama = fmaxf(ama, fabsf(f2lo(pr[j])));
+        amb = fmaxf(amb, fabsf(f2hi(pr[j])));
       }
       const bool blk_ok = t0 + b * 16 < rows;   // rows % 16 == 0: a block is all in or all out
-      const float ama = fmax_abs16(fa), amb = fmax_abs16(fb);
       const uint32_t ca = blk_ok ? block_code(ama, inv_g) : 0u;
       const uint32_t cb = blk_ok ? block_code(amb, inv_g) : 0u;
-      const uint2 pa = encode16(fa, sm.inv_tab[ca], ama);
-      const uint2 pb = encode16(fb, sm.inv_tab[cb], amb);
+      uint2 pa, pb;
+      encode16_two_rows(pr, sm.inv_tab[ca], sm.inv_tab[cb], ama, amb, pa, pb);
       qwa[2 * bi] = pa.x;
       qwa[2 * bi + 1] = pa.y;
       qwb[2 * bi] = pb.x;
