@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define NVFP4B200_API_VERSION 1
+#define NVFP4B200_API_VERSION 2
 
 enum nvfp4b200_status {
   NVFP4B200_OK = 0,
@@ -61,6 +61,20 @@ int nvfp4b200_get_device_error(int* out);
  * counterpart in the reference (its GEMM is a library call).  Returns
  * NVFP4B200_ERR_INVALID_ARG for negative values. */
 int nvfp4b200_set_gemm_max_sms(int max_sms);
+
+/* Gate/up GEMM with the SwiGLU activation in its epilogue (new: the MLP
+ * forward; no counterpart in the reference).  b: [n, k/2] packed, whose rows
+ * interleave gate and up weights in blocks of 128 (rows 256 t .. 256 t + 127
+ * are gate rows 128 t.., the next 128 the matching up rows); n % 256 == 0.
+ * h: bf16 [m, n/2], h[:, 128 t + j] = silu(gate_j) * up_j computed from the
+ * bf16-rounded gate/up values (the product scale_a * scale_b applied first).
+ * gu: bf16 [m, n] gate/up values in b's row order, or NULL (not stored).
+ * ws (2 x u32, zero on entry, left zero) with h_global_scale_out: device
+ * global scale of h, amax(|h|)/(6*448) (1 when the amax is 0 or not finite),
+ * or both NULL. */
+int nvfp4b200_gemm_swiglu(const void* a, const void* b, const void* sfa, const void* sfb, const float* scale_a,
+                          const float* scale_b, void* h, void* gu, uint32_t* ws, float* h_global_scale_out,
+                          int64_t m, int64_t n, int64_t k, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Quantizers                                                               */
@@ -171,15 +185,17 @@ int nvfp4b200_gemm(const void* a, const void* b, const void* sfa, const void* sf
 /* reference's backward is bf16, float4utils.py:653-683)                     */
 /* ------------------------------------------------------------------------ */
 
-/* h = silu(gate) * up with gu bf16 [tokens, 2*ff] = [gate | up] per row,
- * h bf16 [tokens, ff].  If ws and global_scale_out are non-NULL, also
+/* h = silu(gate) * up with gu bf16 [tokens, 2*ff], h bf16 [tokens, ff].
+ * interleave = 0: each gu row is [gate | up]; interleave = 128: gate and up
+ * alternate in blocks of 128 columns (the layout nvfp4b200_gemm_swiglu
+ * writes; ff % 128 == 0).  If ws and global_scale_out are non-NULL, also
  * writes the global scale of h (as nvfp4b200_global_scale). */
-int nvfp4b200_swiglu_fwd(const void* gu, void* h, int64_t tokens, int64_t ff,
+int nvfp4b200_swiglu_fwd(const void* gu, void* h, int64_t tokens, int64_t ff, int interleave,
                          uint32_t* ws, float* global_scale_out, void* stream);
 
 /* d(gate), d(up) of the above given dh bf16 [tokens, ff] -> dgu bf16
- * [tokens, 2*ff].  Optional global scale of dgu as above. */
-int nvfp4b200_swiglu_bwd(const void* gu, const void* dh, void* dgu, int64_t tokens, int64_t ff,
+ * [tokens, 2*ff] in gu's layout.  Optional global scale of dgu as above. */
+int nvfp4b200_swiglu_bwd(const void* gu, const void* dh, void* dgu, int64_t tokens, int64_t ff, int interleave,
                          uint32_t* ws, float* global_scale_out, void* stream);
 
 /* RMSNorm backward for y = (x*inv_rms)*gamma given dy bf16 [rows, k]:

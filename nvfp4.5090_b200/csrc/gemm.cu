@@ -99,6 +99,9 @@ struct Params {
   int64_t sf_atoms;          // scale atoms per 128-row group = ceil(k/64)
   int num_m_tiles, num_n_tiles, num_k_tiles;
   int d_f32, accumulate, epilogue;
+  int swiglu;                // B rows interleaved [gate 128 | up 128] per tile: d = silu(gate)*up
+  int store_gu;              // swiglu: also store the bf16 gate/up tile (tmap_d)
+  uint32_t* h_amax;          // swiglu: atomic max of |h| (float bits), or null
 };
 
 // ---------------------------------------------------------------------------
@@ -310,6 +313,9 @@ __device__ __forceinline__ float apply_epi(float v, int epi) {
   return v;
 }
 
+// sigmoid for SwiGLU, the same expression as the element-wise SwiGLU kernels
+__device__ __forceinline__ float silu_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
@@ -363,7 +369,7 @@ __device__ __forceinline__ void finish64(uint32_t* v, const Params& p, float alp
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-                      const __grid_constant__ CUtensorMap tmap_d,
+                      const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ CUtensorMap tmap_h,
                       const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -400,6 +406,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     prefetch_tmap(&tmap_sfa);
     prefetch_tmap(&tmap_sfb);
     prefetch_tmap(&tmap_d);
+    if (p.swiglu) prefetch_tmap(&tmap_h);
   }
   if (warp == 1) {
     tmem_alloc2(smem_u32(tmem_slot), TMEM_COLS);
@@ -554,7 +561,108 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int64_t colbase = (int64_t)nb * TILE_N + half * 128;
       const uint32_t tbase =
           tmem_base + (buf ? ACC1_COL : 0) + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * 128);
-      if (!p.d_f32) {
+      if (p.swiglu) {
+        // SwiGLU: this warp owns gate columns [64 half, +64) and the matching up
+        // columns [128 + 64 half, +64) of the tile.  The operand holding the
+        // columns shared with the other accumulator buffer is drained first
+        // (buffer 0: the up chunk of half 1; buffer 1: the gate chunk of half
+        // 0), then released.  gate/up are rounded to bf16 (and stored when
+        // asked), h = silu(gate) * up is computed from the rounded values and
+        // stored as bf16; |h| feeds the global amax.
+        const uint32_t obuf = smem_u32(sOut + (warp - 2) * OUT_CHUNK_BYTES);
+        const uint32_t orow = obuf + lane * 128;
+        const int y0 = mb * TILE_M + (int)rank * CTA_M + quad * 32;
+        const uint32_t lane_base = tmem_base + (buf ? ACC1_COL : 0) + ((uint32_t)(quad * 32) << 16);
+        const int up_first = (buf == 0 && half == 1) ? 1 : 0;
+        const int col_first = up_first ? 128 + 64 * half : 64 * half;   // tile columns
+        const int col_second = up_first ? 64 * half : 128 + 64 * half;
+        uint32_t fr[64];   // first operand, bf16-rounded values as float bits
+        __syncwarp();
+        tmem_ld32(lane_base + col_first, fr);
+        tmem_ld32(lane_base + col_first + 32, fr + 32);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(leader_overlap_free);
+        const bool y_ok = y0 < p.m;
+        // bf16-round the first operand; stage and store it as part of gate/up
+        if (lane == 0) bulk_wait_read();
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            w[e] = pack_bf16x2(__uint_as_float(fr[8 * j + 2 * e]) * alpha, __uint_as_float(fr[8 * j + 2 * e + 1]) * alpha);
+            fr[8 * j + 2 * e] = __float_as_uint(bf16lo(w[e]));
+            fr[8 * j + 2 * e + 1] = __float_as_uint(bf16hi(w[e]));
+          }
+          if (p.store_gu) st_shared_v4(orow + ((j ^ (lane & 7)) << 4), w[0], w[1], w[2], w[3]);
+        }
+        if (p.store_gu) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && y_ok) {
+            tma_store_2d(&tmap_d, obuf, (int)(2 * ((int64_t)nb * TILE_N + col_first)), y0);
+            bulk_commit();
+          }
+        }
+        uint32_t hw[32];   // h as packed bf16 pairs (64 values)
+        uint32_t hmax = 0;
+#pragma unroll
+        for (int pp = 0; pp < 2; ++pp) {
+          uint32_t sr[32];
+          tmem_ld32(lane_base + col_second + 32 * pp, sr);
+          tmem_ld_wait();
+          if (pp == 0 && p.store_gu) {
+            if (lane == 0) bulk_wait_read();
+            __syncwarp();
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = 8 * j + 2 * e;   // value index inside this 32-column pass
+              w[e] = pack_bf16x2(__uint_as_float(sr[i]) * alpha, __uint_as_float(sr[i + 1]) * alpha);
+              const float s0 = bf16lo(w[e]), s1 = bf16hi(w[e]);
+              const float f0 = __uint_as_float(fr[32 * pp + i]), f1 = __uint_as_float(fr[32 * pp + i + 1]);
+              const float g0 = up_first ? s0 : f0, g1 = up_first ? s1 : f1;
+              const float u0 = up_first ? f0 : s0, u1 = up_first ? f1 : s1;
+              const uint32_t hv = pack_bf16x2(g0 * silu_sigmoid(g0) * u0, g1 * silu_sigmoid(g1) * u1);
+              hw[16 * pp + 4 * j + e] = hv;
+              uint32_t a = hv & 0x7FFF7FFFu;
+              a &= ~__vcmpgtu2(a, 0x7F807F80u);
+              hmax = max(hmax, max(a & 0xFFFFu, a >> 16));
+            }
+            if (p.store_gu) st_shared_v4(orow + (((4 * pp + j) ^ (lane & 7)) << 4), w[0], w[1], w[2], w[3]);
+          }
+        }
+        if (p.store_gu) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && y_ok) {
+            tma_store_2d(&tmap_d, obuf, (int)(2 * ((int64_t)nb * TILE_N + col_second)), y0);
+            bulk_commit();
+          }
+        }
+        // h: 64 columns at h column 128 nb + 64 half
+        if (lane == 0) bulk_wait_read();
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          st_shared_v4(orow + ((j ^ (lane & 7)) << 4), hw[4 * j], hw[4 * j + 1], hw[4 * j + 2], hw[4 * j + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && y_ok) {
+          tma_store_2d(&tmap_h, obuf, (int)(2 * ((int64_t)nb * (TILE_N / 2) + 64 * half)), y0);
+          bulk_commit();
+        }
+        if (p.h_amax) {
+          hmax = __reduce_max_sync(0xffffffffu, row_ok ? hmax : 0u);
+          if (lane == 0 && hmax) atomicMax(p.h_amax, hmax << 16);
+        }
+      } else if (!p.d_f32) {
         // bf16: each 32-row x 64-column chunk goes through this warp's shared
         // staging buffer (128-byte swizzle: 16-byte piece j of row i at
         // (j ^ (i % 8)) * 16) and out with one TMA store, which drops rows and
@@ -738,9 +846,24 @@ static DeviceInfo device_info() {
   return d;
 }
 
+// SwiGLU outputs of the gate/up GEMM (nvfp4b200_gemm_swiglu): d is h [m, n/2].
+struct SwigluOut {
+  void* gu;          // bf16 [m, n] gate/up (interleaved like B's rows), or null
+  uint32_t* ws;      // 2-word amax workspace (zero on entry and on return), or null
+  float* g_out;      // global scale of h = amax(h) / (6 * 448), or null
+};
+
+// g = amax / 2688 from the amax bits in ws[0] (1 when 0 or not finite); resets ws[0].
+__global__ void h_scale_finalize_kernel(uint32_t* ws, float* g_out) {
+  const float amax = __uint_as_float(ws[0]);
+  *g_out = (amax > 0.0f && amax <= 3.402823466e38f) ? __fdiv_rn(amax, 2688.0f) : 1.0f;
+  ws[0] = 0u;
+}
+
 static int run(const void* a, const void* b, const void* sfa, const void* sfb, const float* scale_a,
                const float* scale_b, const void* bias, const void* residual, void* d, int d_dtype, int accumulate,
-               int epilogue, int64_t m, int64_t n, int64_t k, int64_t ldd, cudaStream_t stream) {
+               int epilogue, int64_t m, int64_t n, int64_t k, int64_t ldd, cudaStream_t stream,
+               const SwigluOut* sw = nullptr) {
   if (!a || !b || !sfa || !sfb || !d) return NVFP4B200_ERR_INVALID_ARG;
   if (d_dtype != NVFP4B200_BF16 && d_dtype != NVFP4B200_F32) return NVFP4B200_ERR_INVALID_ARG;
   if (epilogue < 0 || epilogue > 2) return NVFP4B200_ERR_INVALID_ARG;
@@ -767,9 +890,18 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
       !make_map(&msb, sfb, pad_n * sf_atoms * 4 / 256, 256, 256, 2 * KBLOCKS, CU_TENSOR_MAP_SWIZZLE_NONE))
     return NVFP4B200_ERR_CUDA;
   // bf16 output viewed as bytes: [m rows, 2n bytes], row stride 2*ldd, boxes of 32 rows x 128 bytes
-  if (d_dtype == NVFP4B200_BF16 && !make_map(&md, d, m, 2 * n, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B, 2 * ldd))
-    return NVFP4B200_ERR_CUDA;
-  if (d_dtype == NVFP4B200_F32 && !make_map_f32(&md, d, m, n, ldd)) return NVFP4B200_ERR_CUDA;
+  CUtensorMap mh;
+  memset(&mh, 0, sizeof(mh));
+  if (sw) {
+    // h [m, n/2] and the optional gate/up [m, n], both bf16 viewed as bytes
+    if (!make_map(&mh, d, m, n, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B, n)) return NVFP4B200_ERR_CUDA;
+    if (sw->gu && !make_map(&md, sw->gu, m, 2 * n, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B, 2 * n))
+      return NVFP4B200_ERR_CUDA;
+  } else {
+    if (d_dtype == NVFP4B200_BF16 && !make_map(&md, d, m, 2 * n, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B, 2 * ldd))
+      return NVFP4B200_ERR_CUDA;
+    if (d_dtype == NVFP4B200_F32 && !make_map_f32(&md, d, m, n, ldd)) return NVFP4B200_ERR_CUDA;
+  }
   Params p;
   p.scale_a = scale_a;
   p.scale_b = scale_b;
@@ -787,6 +919,9 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   p.d_f32 = d_dtype == NVFP4B200_F32;
   p.accumulate = accumulate;
   p.epilogue = epilogue;
+  p.swiglu = sw ? 1 : 0;
+  p.store_gu = (sw && sw->gu) ? 1 : 0;
+  p.h_amax = sw ? sw->ws : nullptr;
   const int64_t tiles = (int64_t)p.num_m_tiles * p.num_n_tiles;
   const DeviceInfo info = device_info();
   int cap = info.max_clusters;
@@ -796,7 +931,12 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   if (cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
       cudaSuccess)
     return NVFP4B200_ERR_CUDA;
-  nvfp4_gemm_kernel<<<2 * clusters, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, msa, msb, md, p);
+  nvfp4_gemm_kernel<<<2 * clusters, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, msa, msb, md, mh, p);
+  if (sw && sw->ws) {
+    const int lrc = launch_status();
+    if (lrc) return lrc;
+    h_scale_finalize_kernel<<<1, 1, 0, stream>>>(sw->ws, sw->g_out);
+  }
   return launch_status();
 }
 
@@ -832,6 +972,17 @@ int nvfp4b200_gemm(const void* a, const void* b, const void* sfa, const void* sf
                    int accumulate, int epilogue, int64_t m, int64_t n, int64_t k, int64_t ldd, void* stream) {
   return gemm::run(a, b, sfa, sfb, scale_a, scale_b, bias, residual, d, d_dtype, accumulate, epilogue, m, n, k, ldd,
                    (cudaStream_t)stream);
+}
+
+int nvfp4b200_gemm_swiglu(const void* a, const void* b, const void* sfa, const void* sfb, const float* scale_a,
+                          const float* scale_b, void* h, void* gu, uint32_t* ws, float* h_global_scale_out, int64_t m,
+                          int64_t n, int64_t k, void* stream) {
+  if (!h || (ws == nullptr) != (h_global_scale_out == nullptr)) return NVFP4B200_ERR_INVALID_ARG;
+  if (n <= 0 || n % gemm::TILE_N) return NVFP4B200_ERR_BAD_SHAPE;   // whole gate|up tiles
+  if ((gu && !aligned(gu, 16)) || (ws && !aligned(ws, 4))) return NVFP4B200_ERR_MISALIGNED;
+  gemm::SwigluOut sw{gu, ws, h_global_scale_out};
+  return gemm::run(a, b, sfa, sfb, scale_a, scale_b, nullptr, nullptr, h, NVFP4B200_BF16, 0, NVFP4B200_EPI_NONE, m, n,
+                   k, n, (cudaStream_t)stream, &sw);
 }
 
 int nvfp4b200_nvfp4_mm(const void* a, const void* b, const void* sfa, const void* sfb, const float* output_scale,

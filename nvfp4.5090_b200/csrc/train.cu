@@ -39,17 +39,25 @@ __device__ __forceinline__ uint32_t absmax_word_bits(uint32_t w) {
   return max(a & 0xFFFFu, a >> 16) << 16;
 }
 
-// h = silu(gate) * up with gu = [gate | up] per row; optional global amax of
-// h.  CTAs stride over rows, threads over 8-column vectors of a row.
+// Column of gate value c in a gu row, and the distance to its up value:
+// [gate | up] halves (il = 0) or blocks of 128 alternating (il = 128).
+__device__ __forceinline__ int64_t gate_col(int64_t c, int il) { return il ? ((c >> 7) << 8) + (c & 127) : c; }
+
+// h = silu(gate) * up with gu = [gate | up] per row (or interleaved blocks);
+// optional global amax of h.  CTAs stride over rows, threads over 8-column
+// vectors of a row (a vector never straddles a 128-column block).
 __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const uint16_t* __restrict__ gu, uint16_t* __restrict__ h,
-                                                         int64_t tokens, int64_t ff, uint32_t* ws, float* g_out) {
+                                                         int64_t tokens, int64_t ff, int il, uint32_t* ws,
+                                                         float* g_out) {
+  const int64_t up_off = il ? 128 : ff;
   uint32_t m = 0;
   for (int64_t t = blockIdx.x; t < tokens; t += gridDim.x) {
     const uint16_t* grow = gu + t * 2 * ff;
     uint16_t* hrow = h + t * ff;
     for (int64_t c = 8 * (int64_t)threadIdx.x; c < ff; c += 8 * (int64_t)blockDim.x) {
-      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(grow + c));
-      const uint4 uv = __ldg(reinterpret_cast<const uint4*>(grow + ff + c));
+      const int64_t gc = gate_col(c, il);
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(grow + gc));
+      const uint4 uv = __ldg(reinterpret_cast<const uint4*>(grow + gc + up_off));
       const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
       uint32_t o[4];
 #pragma unroll
@@ -70,15 +78,18 @@ __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const uint16_t* __restr
 // silu'(g) = s * (1 + g * (1 - s)), s = sigmoid(g).
 __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint16_t* __restrict__ gu,
                                                          const uint16_t* __restrict__ dh, uint16_t* __restrict__ dgu,
-                                                         int64_t tokens, int64_t ff, uint32_t* ws, float* g_out) {
+                                                         int64_t tokens, int64_t ff, int il, uint32_t* ws,
+                                                         float* g_out) {
+  const int64_t up_off = il ? 128 : ff;
   uint32_t m = 0;
   for (int64_t t = blockIdx.x; t < tokens; t += gridDim.x) {
     const uint16_t* grow = gu + t * 2 * ff;
     const uint16_t* drow = dh + t * ff;
     uint16_t* orow = dgu + t * 2 * ff;
     for (int64_t c = 8 * (int64_t)threadIdx.x; c < ff; c += 8 * (int64_t)blockDim.x) {
-      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(grow + c));
-      const uint4 uv = __ldg(reinterpret_cast<const uint4*>(grow + ff + c));
+      const int64_t gc = gate_col(c, il);
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(grow + gc));
+      const uint4 uv = __ldg(reinterpret_cast<const uint4*>(grow + gc + up_off));
       const uint4 dv = __ldg(reinterpret_cast<const uint4*>(drow + c));
       const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w},
                      dw[4] = {dv.x, dv.y, dv.z, dv.w};
@@ -99,8 +110,8 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint16_t* __restr
         ou[j] = pack2(du[0], du[1]);
         m = max(m, max(absmax_word_bits(og[j]), absmax_word_bits(ou[j])));
       }
-      *reinterpret_cast<uint4*>(orow + c) = make_uint4(og[0], og[1], og[2], og[3]);
-      *reinterpret_cast<uint4*>(orow + ff + c) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+      *reinterpret_cast<uint4*>(orow + gc) = make_uint4(og[0], og[1], og[2], og[3]);
+      *reinterpret_cast<uint4*>(orow + gc + up_off) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
     }
   }
   if (ws) amax_commit(m, ws, g_out, nullptr);
@@ -298,32 +309,34 @@ using namespace nvfp4b200;
 
 extern "C" {
 
-int nvfp4b200_swiglu_fwd(const void* gu, void* h, int64_t tokens, int64_t ff, uint32_t* ws, float* global_scale_out,
-                         void* stream) {
+int nvfp4b200_swiglu_fwd(const void* gu, void* h, int64_t tokens, int64_t ff, int interleave, uint32_t* ws,
+                         float* global_scale_out, void* stream) {
   if (!gu || !h) return NVFP4B200_ERR_INVALID_ARG;
   if ((ws == nullptr) != (global_scale_out == nullptr)) return NVFP4B200_ERR_INVALID_ARG;
-  if (tokens < 0 || ff <= 0 || ff % 8) return NVFP4B200_ERR_BAD_SHAPE;
+  if (interleave != 0 && interleave != 128) return NVFP4B200_ERR_INVALID_ARG;
+  if (tokens < 0 || ff <= 0 || ff % 8 || (interleave && ff % 128)) return NVFP4B200_ERR_BAD_SHAPE;
   if (!aligned(gu, 16) || !aligned(h, 16)) return NVFP4B200_ERR_MISALIGNED;
   int rc = check_device();
   if (rc) return rc;
   if (tokens == 0) return NVFP4B200_OK;
   swiglu_fwd_kernel<<<(unsigned)std::min<int64_t>(tokens, (int64_t)sm_count() * 8), 256, 0, (cudaStream_t)stream>>>(
-      static_cast<const uint16_t*>(gu), static_cast<uint16_t*>(h), tokens, ff, ws, global_scale_out);
+      static_cast<const uint16_t*>(gu), static_cast<uint16_t*>(h), tokens, ff, interleave, ws, global_scale_out);
   return launch_status();
 }
 
-int nvfp4b200_swiglu_bwd(const void* gu, const void* dh, void* dgu, int64_t tokens, int64_t ff, uint32_t* ws,
-                         float* global_scale_out, void* stream) {
+int nvfp4b200_swiglu_bwd(const void* gu, const void* dh, void* dgu, int64_t tokens, int64_t ff, int interleave,
+                         uint32_t* ws, float* global_scale_out, void* stream) {
   if (!gu || !dh || !dgu) return NVFP4B200_ERR_INVALID_ARG;
   if ((ws == nullptr) != (global_scale_out == nullptr)) return NVFP4B200_ERR_INVALID_ARG;
-  if (tokens < 0 || ff <= 0 || ff % 8) return NVFP4B200_ERR_BAD_SHAPE;
+  if (interleave != 0 && interleave != 128) return NVFP4B200_ERR_INVALID_ARG;
+  if (tokens < 0 || ff <= 0 || ff % 8 || (interleave && ff % 128)) return NVFP4B200_ERR_BAD_SHAPE;
   if (!aligned(gu, 16) || !aligned(dh, 16) || !aligned(dgu, 16)) return NVFP4B200_ERR_MISALIGNED;
   int rc = check_device();
   if (rc) return rc;
   if (tokens == 0) return NVFP4B200_OK;
   swiglu_bwd_kernel<<<(unsigned)std::min<int64_t>(tokens, (int64_t)sm_count() * 8), 256, 0, (cudaStream_t)stream>>>(
-      static_cast<const uint16_t*>(gu), static_cast<const uint16_t*>(dh), static_cast<uint16_t*>(dgu), tokens, ff, ws,
-      global_scale_out);
+      static_cast<const uint16_t*>(gu), static_cast<const uint16_t*>(dh), static_cast<uint16_t*>(dgu), tokens, ff,
+      interleave, ws, global_scale_out);
   return launch_status();
 }
 

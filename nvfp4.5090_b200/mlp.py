@@ -22,6 +22,13 @@ Q quantizes along rows' last dimension, Q_t along the first (transposed
 quantizer).  Quantization is treated as identity in the backward
 (straight-through).  Weights are quantized once per optimizer step and
 reused across micro-batches.
+
+W_gu's 2F rows may be stored [W_gate; W_up] (``interleave=0``) or with gate
+and up rows alternating in blocks of 128 (``interleave=128``).  The latter
+lets the gate/up GEMM apply SwiGLU in its epilogue (each 256-column output
+tile holds 128 gate columns and their up columns), so h and its global
+scale come out of that GEMM; every other GEMM only sees a relabelled 2F
+dimension.  NVFP4MLPStackTrainer keeps W_gu interleaved.
 """
 from __future__ import annotations
 
@@ -74,13 +81,21 @@ class Saved:
     g_h: torch.Tensor
 
 
-def block_forward(x: torch.Tensor, gamma: torch.Tensor, qw: QWeights, eps: float = 1e-6, save: bool = True):
-    """One RMSNorm+SwiGLU block on bf16 x [T, D] -> (y [T, D], saved activations)."""
+def block_forward(x: torch.Tensor, gamma: torch.Tensor, qw: QWeights, eps: float = 1e-6, save: bool = True,
+                  interleave: int = 0):
+    """One RMSNorm+SwiGLU block on bf16 x [T, D] -> (y [T, D], saved activations).
+
+    ``interleave=128``: W_gu rows alternate gate/up in blocks of 128 and the
+    gate/up GEMM computes h in its epilogue."""
     inv_rms, g_xn = ops.rmsnorm_stats(x, eps, gamma=gamma)
     q_xn, s_xn = ops.quantize(x, global_scale=g_xn, row_scale=inv_rms, gamma=gamma)
-    gu = ops.gemm(q_xn, s_xn, qw.q_gu, qw.s_gu, scale_a=g_xn, scale_b=qw.g_gu)
-    del q_xn, s_xn
-    h, g_h = ops.swiglu_fwd(gu, with_scale=True)
+    if interleave:
+        h, gu, g_h = ops.gemm_swiglu(q_xn, s_xn, qw.q_gu, qw.s_gu, scale_a=g_xn, scale_b=qw.g_gu, store_gu=save)
+        del q_xn, s_xn
+    else:
+        gu = ops.gemm(q_xn, s_xn, qw.q_gu, qw.s_gu, scale_a=g_xn, scale_b=qw.g_gu)
+        del q_xn, s_xn
+        h, g_h = ops.swiglu_fwd(gu, with_scale=True)
     q_h, s_h = ops.quantize(h, global_scale=g_h)
     y = ops.gemm(q_h, s_h, qw.q_down, qw.s_down, scale_a=g_h, scale_b=qw.g_down, residual=x)
     saved = Saved(x, inv_rms, g_xn, gu, h, g_h) if save else None
@@ -89,7 +104,7 @@ def block_forward(x: torch.Tensor, gamma: torch.Tensor, qw: QWeights, eps: float
 
 def block_backward(dy: torch.Tensor, gamma: torch.Tensor, qw: QWeights, sv: Saved,
                    grad_gamma: torch.Tensor, grad_gu: torch.Tensor, grad_down: torch.Tensor,
-                   accumulate: bool) -> torch.Tensor:
+                   accumulate: bool, interleave: int = 0) -> torch.Tensor:
     """Backward of block_forward given dy [T, D].
 
     grad_gamma (fp32 [D]) is accumulated; grad_gu ([2F, D]) and grad_down
@@ -104,7 +119,7 @@ def block_backward(dy: torch.Tensor, gamma: torch.Tensor, qw: QWeights, sv: Save
     q_ht, s_ht = ops.quantize_t(sv.h, global_scale=sv.g_h)
     ops.gemm(q_dyt, s_dyt, q_ht, s_ht, scale_a=g_dy, scale_b=sv.g_h, out=grad_down, accumulate=accumulate)
     del q_dyt, s_dyt, q_ht, s_ht
-    dgu, g_dgu = ops.swiglu_bwd(sv.gu, dh, with_scale=True)
+    dgu, g_dgu = ops.swiglu_bwd(sv.gu, dh, with_scale=True, interleave=interleave)
     del dh
     q_dgu, s_dgu = ops.quantize(dgu, global_scale=g_dgu)
     dxn = ops.gemm(q_dgu, s_dgu, qw.q_gu_t, qw.s_gu_t, scale_a=g_dgu, scale_b=qw.g_gu)
@@ -261,6 +276,8 @@ class NVFP4MLPStackTrainer:
             if world > 1:
                 self.reducer = BucketAllReducer(process_group)
         self.step_count = 0
+        # W_gu rows interleave gate/up in blocks of 128 (fused SwiGLU epilogue) when F allows
+        self.interleave = 128 if d_ff % 128 == 0 else 0
         # SMs left to the gradient collectives while the step's GEMMs run (DP only)
         self.comm_sms = comm_sms if world > 1 else 0
         self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
@@ -298,7 +315,7 @@ class NVFP4MLPStackTrainer:
             h = x[lo:hi]
             saved: List[Saved] = []
             for bi, b in enumerate(self.blocks):
-                h, sv = block_forward(h, b.gamma, qw(bi), self.eps)
+                h, sv = block_forward(h, b.gamma, qw(bi), self.eps, interleave=self.interleave)
                 saved.append(sv)
             out_sum += h.sum(dtype=torch.float32)
             g = dy[lo:hi]
@@ -307,11 +324,11 @@ class NVFP4MLPStackTrainer:
                 b = self.blocks[bi]
                 if n_micro == 1:
                     g = block_backward(g, b.gamma, qws[bi], saved[bi], b.grad_gamma32, b.grad_gu, b.grad_down,
-                                       accumulate=False)
+                                       accumulate=False, interleave=self.interleave)
                 else:
                     # the first micro-batch writes the fp32 accumulators, later ones add to them
                     g = block_backward(g, b.gamma, qws[bi], saved[bi], b.grad_gamma32, b.acc_gu, b.acc_down,
-                                       accumulate=mi > 0)
+                                       accumulate=mi > 0, interleave=self.interleave)
                     if last:
                         b.grad_gu.copy_(b.acc_gu)
                         b.grad_down.copy_(b.acc_down)

@@ -220,19 +220,21 @@ def gemm(qa: torch.Tensor, sa: torch.Tensor, qb: torch.Tensor, sb: torch.Tensor,
 # ----------------------------------------------------------------------------
 
 
-def swiglu_fwd(gu: torch.Tensor, with_scale: bool = False):
-    """h = silu(gate)*up for gu = [gate | up] bf16 [T, 2F]; optionally also g(h)."""
+def swiglu_fwd(gu: torch.Tensor, with_scale: bool = False, interleave: int = 0):
+    """h = silu(gate)*up for gu bf16 [T, 2F] ([gate | up] per row, or gate/up
+    alternating in blocks of ``interleave`` = 128 columns); optionally also g(h)."""
     _check_bf16(gu, "swiglu_fwd")
     t, f2 = gu.shape
     f = f2 // 2
     h = torch.empty((t, f), device=gu.device, dtype=torch.bfloat16)
     g = torch.empty((1,), device=gu.device, dtype=torch.float32) if with_scale else None
     ws = workspace(gu.device) if with_scale else None
-    _lib.call("nvfp4b200_swiglu_fwd", gu.data_ptr(), h.data_ptr(), t, f, _ptr(ws), _ptr(g), _stream(gu))
+    _lib.call("nvfp4b200_swiglu_fwd", gu.data_ptr(), h.data_ptr(), t, f, int(interleave), _ptr(ws), _ptr(g),
+              _stream(gu))
     return (h, g) if with_scale else h
 
 
-def swiglu_bwd(gu: torch.Tensor, dh: torch.Tensor, with_scale: bool = False):
+def swiglu_bwd(gu: torch.Tensor, dh: torch.Tensor, with_scale: bool = False, interleave: int = 0):
     _check_bf16(gu, "swiglu_bwd")
     t, f2 = gu.shape
     f = f2 // 2
@@ -240,9 +242,35 @@ def swiglu_bwd(gu: torch.Tensor, dh: torch.Tensor, with_scale: bool = False):
     dgu = torch.empty_like(gu)
     g = torch.empty((1,), device=gu.device, dtype=torch.float32) if with_scale else None
     ws = workspace(gu.device) if with_scale else None
-    _lib.call("nvfp4b200_swiglu_bwd", gu.data_ptr(), dh.data_ptr(), dgu.data_ptr(), t, f, _ptr(ws), _ptr(g),
-              _stream(gu))
+    _lib.call("nvfp4b200_swiglu_bwd", gu.data_ptr(), dh.data_ptr(), dgu.data_ptr(), t, f, int(interleave), _ptr(ws),
+              _ptr(g), _stream(gu))
     return (dgu, g) if with_scale else dgu
+
+
+def gemm_swiglu(qa: torch.Tensor, sa: torch.Tensor, qb: torch.Tensor, sb: torch.Tensor, *,
+                scale_a: Optional[torch.Tensor] = None, scale_b: Optional[torch.Tensor] = None,
+                store_gu: bool = True, with_scale: bool = True):
+    """Gate/up GEMM with SwiGLU in the epilogue.  qb's rows interleave gate and
+    up weights in blocks of 128.  Returns (h [m, n/2], gu [m, n] or None,
+    g(h) or None), all bf16 except the fp32 global scale."""
+    _require(qa.is_cuda and qb.is_cuda, "gemm_swiglu requires CUDA tensors")
+    m, kh = qa.shape
+    n, kh2 = qb.shape
+    _require(kh == kh2, f"K mismatch: A has {2 * kh}, B has {2 * kh2}")
+    _require(n % 256 == 0, "gemm_swiglu needs n (= 2F) % 256 == 0")
+    k = 2 * kh
+    _require(qa.is_contiguous() and qb.is_contiguous() and sa.is_contiguous() and sb.is_contiguous(),
+             "gemm operands must be contiguous")
+    _require(sa.numel() == math.prod(scale_shape(m, k)) and sb.numel() == math.prod(scale_shape(n, k)),
+             "scale tensors must be the padded swizzled [round_up(rows,128), round_up(k/16,4)] layout")
+    h = torch.empty((m, n // 2), device=qa.device, dtype=torch.bfloat16)
+    gu = torch.empty((m, n), device=qa.device, dtype=torch.bfloat16) if store_gu else None
+    g = torch.empty((1,), device=qa.device, dtype=torch.float32) if with_scale else None
+    ws = workspace(qa.device) if with_scale else None
+    _lib.call("nvfp4b200_gemm_swiglu", qa.data_ptr(), qb.data_ptr(), sa.data_ptr(), sb.data_ptr(),
+              _ptr(_scalar_f32(scale_a, qa.device)), _ptr(_scalar_f32(scale_b, qa.device)), h.data_ptr(), _ptr(gu),
+              _ptr(ws), _ptr(g), m, n, k, _stream(qa))
+    return h, gu, g
 
 
 def rmsnorm_bwd(x: torch.Tensor, gamma: Optional[torch.Tensor], inv_rms: torch.Tensor, dy: torch.Tensor,

@@ -61,7 +61,13 @@ MIS = FAKE + 4
     (lambda L: L.nvfp4b200_nvfp4_mm(None, FAKE, FAKE, FAKE, None, None, FAKE, 8, 8, 64, None), 1),
     (lambda L: L.nvfp4b200_gemm(FAKE, FAKE, FAKE, FAKE, None, None, None, None, FAKE, 0, 1, 0, 8, 8, 64, 8, None), 1),
     (lambda L: L.nvfp4b200_gemm(FAKE, FAKE, FAKE, FAKE, None, None, None, None, FAKE, 0, 0, 7, 8, 8, 64, 8, None), 1),
-    (lambda L: L.nvfp4b200_swiglu_fwd(FAKE, FAKE, 4, 12, None, None, None), 2),
+    (lambda L: L.nvfp4b200_swiglu_fwd(FAKE, FAKE, 4, 12, 0, None, None, None), 2),       # ff % 8
+    (lambda L: L.nvfp4b200_swiglu_fwd(FAKE, FAKE, 4, 64, 128, None, None, None), 2),     # interleaved ff % 128
+    (lambda L: L.nvfp4b200_swiglu_bwd(FAKE, FAKE, FAKE, 4, 64, 7, None, None, None), 1),  # bad interleave
+    (lambda L: L.nvfp4b200_gemm_swiglu(FAKE, FAKE, FAKE, FAKE, None, None, FAKE, None, None, None, 8, 384, 64,
+                                       None), 2),                                         # n % 256
+    (lambda L: L.nvfp4b200_gemm_swiglu(FAKE, FAKE, FAKE, FAKE, None, None, FAKE, None, FAKE, None, 8, 512, 64,
+                                       None), 1),                                         # ws without g_out
     (lambda L: L.nvfp4b200_adamw_step(FAKE, FAKE, 5, FAKE, FAKE, 8, 1e-3, .9, .95, 1e-8, 0., 1., 1., 1., None), 1),
 ])
 def test_argument_validation_without_device(pkg, call, expected):

@@ -93,10 +93,11 @@ def test_stack_trainer_microbatch_accumulation_is_exact_sum(pkg):
     acc_dn = torch.zeros(d, f, device="cuda")
     acc_gam = torch.zeros(d, device="cuda")
     for lo in (0, 256):
-        y, sv = mlp.block_forward(x[lo:lo + 256], blk.gamma, qw)
+        y, sv = mlp.block_forward(x[lo:lo + 256], blk.gamma, qw, interleave=tr.interleave)
         ggu = torch.empty(2 * f, d, device="cuda")
         gdn = torch.empty(d, f, device="cuda")
-        mlp.block_backward(dy[lo:lo + 256], blk.gamma, qw, sv, acc_gam, ggu, gdn, accumulate=False)
+        mlp.block_backward(dy[lo:lo + 256], blk.gamma, qw, sv, acc_gam, ggu, gdn, accumulate=False,
+                           interleave=tr.interleave)
         acc_gu += ggu
         acc_dn += gdn
     r = tr.step(x, dy)
@@ -130,3 +131,86 @@ def test_stack_trainer_full_batch_vs_microbatch_consistent(pkg):
         ga, gb = ba.grad.float(), bb.grad.float()
         assert ((ga - gb).norm() / ga.norm()).item() < 0.3
         assert torch.nn.functional.cosine_similarity(ga, gb, dim=0).item() > 0.95
+
+
+def _interleave_rows(w_gu: torch.Tensor) -> torch.Tensor:
+    """[W_gate; W_up] (2F rows) -> gate/up rows alternating in blocks of 128."""
+    f = w_gu.shape[0] // 2
+    idx = []
+    for t in range(f // 128):
+        idx += list(range(128 * t, 128 * t + 128)) + list(range(f + 128 * t, f + 128 * t + 128))
+    return w_gu[torch.tensor(idx, device=w_gu.device)]
+
+
+def _interleave_cols(gu: torch.Tensor) -> torch.Tensor:
+    return _interleave_rows(gu.t().contiguous()).t().contiguous()
+
+
+def test_gemm_swiglu_equals_gemm_then_swiglu(pkg):
+    """The SwiGLU epilogue gives bit-identical gate/up, h and global scale of h
+    to the plain GEMM followed by the element-wise SwiGLU kernel."""
+    m, f, k = 300, 512, 384
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    a = torch.randn(m, k, device="cuda", generator=gen).to(torch.bfloat16)
+    w = (0.05 * torch.randn(2 * f, k, device="cuda", generator=gen)).to(torch.bfloat16)
+    ga, gw = pkg.ops.global_scale(a), pkg.ops.global_scale(w)
+    qa, sa = pkg.ops.quantize(a, global_scale=ga)
+    qw, sw = pkg.ops.quantize(w, global_scale=gw)
+    h, gu, gh = pkg.ops.gemm_swiglu(qa, sa, qw, sw, scale_a=ga, scale_b=gw)
+    gu_ref = pkg.ops.gemm(qa, sa, qw, sw, scale_a=ga, scale_b=gw)
+    h_ref, gh_ref = pkg.ops.swiglu_fwd(gu_ref, with_scale=True, interleave=128)
+    torch.cuda.synchronize()
+    assert pkg.ops.device_error() == 0
+    assert torch.equal(gu.view(torch.int16), gu_ref.view(torch.int16))
+    assert torch.equal(h.view(torch.int16), h_ref.view(torch.int16))
+    assert torch.equal(gh, gh_ref)
+    h2, gu2, g2 = pkg.ops.gemm_swiglu(qa, sa, qw, sw, scale_a=ga, scale_b=gw, store_gu=False, with_scale=False)
+    assert gu2 is None and g2 is None and torch.equal(h2.view(torch.int16), h_ref.view(torch.int16))
+
+
+def test_swiglu_interleaved_layout_equals_halves(pkg):
+    t, f = 96, 256
+    gen = torch.Generator(device="cuda").manual_seed(12)
+    gu = torch.randn(t, 2 * f, device="cuda", generator=gen).to(torch.bfloat16)
+    dh = (0.1 * torch.randn(t, f, device="cuda", generator=gen)).to(torch.bfloat16)
+    h0, g0 = pkg.ops.swiglu_fwd(gu, with_scale=True)
+    h1, g1 = pkg.ops.swiglu_fwd(_interleave_cols(gu), with_scale=True, interleave=128)
+    assert torch.equal(h0.view(torch.int16), h1.view(torch.int16)) and torch.equal(g0, g1)
+    d0, gd0 = pkg.ops.swiglu_bwd(gu, dh, with_scale=True)
+    d1, gd1 = pkg.ops.swiglu_bwd(_interleave_cols(gu), dh, with_scale=True, interleave=128)
+    assert torch.equal(_interleave_cols(d0).view(torch.int16), d1.view(torch.int16)) and torch.equal(gd0, gd1)
+
+
+def test_block_fused_swiglu_equals_unfused(pkg):
+    """A block with interleaved W_gu (SwiGLU in the GEMM epilogue) against the
+    same block with [W_gate; W_up]: forward bit-identical; backward identical up
+    to the row permutation except dx/dgamma, whose dgrad GEMM contracts over
+    the permuted 2F dimension (fp32 summation order)."""
+    import importlib
+    mlp = importlib.import_module("nvfp4_b200.mlp")
+    t, d, f = 256, 256, 512
+    gen = torch.Generator(device="cuda").manual_seed(13)
+    x = torch.randn(t, d, device="cuda", generator=gen).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(d, device="cuda", generator=gen)).to(torch.bfloat16)
+    w_gu = (0.02 * torch.randn(2 * f, d, device="cuda", generator=gen)).to(torch.bfloat16)
+    w_down = (0.02 * torch.randn(d, f, device="cuda", generator=gen)).to(torch.bfloat16)
+    dy = (1e-3 * torch.randn(t, d, device="cuda", generator=gen)).to(torch.bfloat16)
+    w_il = _interleave_rows(w_gu)
+    outs = []
+    for wg, il in ((w_gu, 0), (w_il, 128)):
+        qw = mlp.quantize_weights(wg, w_down)
+        y, sv = mlp.block_forward(x, gamma, qw, interleave=il)
+        gg = torch.zeros(d, device="cuda")
+        dgu = torch.empty(2 * f, d, device="cuda", dtype=torch.bfloat16)
+        dd = torch.empty(d, f, device="cuda", dtype=torch.bfloat16)
+        dx = mlp.block_backward(dy, gamma, qw, sv, gg, dgu, dd, accumulate=False, interleave=il)
+        outs.append((y, sv.h, dx, gg, dgu, dd))
+    torch.cuda.synchronize()
+    assert pkg.ops.device_error() == 0
+    (y0, h0, dx0, gg0, dgu0, dd0), (y1, h1, dx1, gg1, dgu1, dd1) = outs
+    assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))
+    assert torch.equal(h0.view(torch.int16), h1.view(torch.int16))
+    assert torch.equal(dd0.view(torch.int16), dd1.view(torch.int16))
+    assert torch.equal(_interleave_rows(dgu0).view(torch.int16), dgu1.view(torch.int16))
+    rel = lambda a, b: ((a.float() - b.float()).norm() / b.float().norm()).item()
+    assert rel(dx1, dx0) < 1e-2 and rel(gg1, gg0) < 1e-2
