@@ -202,11 +202,26 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       "l"(map), "r"(bar), "r"(x), "r"(y)
       : "memory");
 }
-// 2-D tiled TMA store of a shared-memory box (bulk async-group of the issuing thread).
+// 3-D tiled TMA load, otherwise as tma_load_2d_pair.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y,
+                                                 int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(map), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+// 2-D tiled TMA store of a shared-memory box (bulk async-group of the issuing
+// thread).  The output is marked evict-first in L2: it is not read again by
+// this kernel, and keeping the operand tiles resident instead measured 0.3-2%
+// faster (8192^3 to 16384^3).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),
-               "r"(x), "r"(y)
-               : "memory");
+  asm volatile(
+      "{\n\t.reg .b64 pol;\n\t"
+      "createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], pol;\n\t}" ::"l"(map),
+      "r"(src), "r"(x), "r"(y)
+      : "memory");
 }
 // 2-D tiled TMA reduce-add of a shared-memory box into global memory (the
 // element type, f32 here, comes from the tensor map; L2 performs the add).
@@ -435,8 +450,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int b_row = nb * TILE_N + (int)rank * CTA_N;
       // scale slabs are rows of 256 bytes; slab (group, kt) starts at row (group * atoms + 4 * kt) * 2
       const int64_t sfa_row0 = ((int64_t)(2 * mb + (int)rank) * p.sf_atoms) * 2;
-      const int64_t sfb_row0 = ((int64_t)(2 * nb) * p.sf_atoms) * 2;
-      const int64_t sfb_row1 = ((int64_t)(2 * nb + 1) * p.sf_atoms) * 2;
       for (int kt = 0; kt < p.num_k_tiles; ++kt) {
         if (!warp_wait(empty_bar(stage), phase ^ 1, abort_flag)) {
           ok = false;
@@ -449,8 +462,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           tma_load_2d_pair(smem_u32(sA + stage * A_BYTES), &tmap_a, lbar, kt * BK_BYTES, a_row);
           tma_load_2d_pair(smem_u32(sB + stage * B_BYTES), &tmap_b, lbar, kt * BK_BYTES, b_row);
           tma_load_2d_pair(smem_u32(sSFA + stage * SFA_BYTES), &tmap_sfa, lbar, 0, (int)(sfa_row0 + sf_dy));
-          tma_load_2d_pair(smem_u32(sSFB + stage * SFB_BYTES), &tmap_sfb, lbar, 0, (int)(sfb_row0 + sf_dy));
-          tma_load_2d_pair(smem_u32(sSFB + stage * SFB_BYTES + SFB_G1), &tmap_sfb, lbar, 0, (int)(sfb_row1 + sf_dy));
+          // both 128-row scale groups of the B tile in one load (3-D map: bytes, slab rows, group)
+          tma_load_3d_pair(smem_u32(sSFB + stage * SFB_BYTES), &tmap_sfb, lbar, 0, sf_dy, 2 * nb);
         }
         __syncwarp();
         armed |= 1u << stage;
@@ -805,6 +818,21 @@ static bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t r
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Scale tensor as [groups][rows_per_group][256 bytes] (a 128-row group's
+// atoms are rows_per_group rows of 256 bytes); one box = one k-slab
+// (2 * KBLOCKS rows) of two consecutive groups.  Groups past the end read zeros.
+static bool make_map_sf_groups(CUtensorMap* map, const void* base, int64_t groups, int64_t rows_per_group) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {256, (cuuint64_t)rows_per_group, (cuuint64_t)groups};
+  cuuint64_t strides[2] = {256, (cuuint64_t)(rows_per_group * 256)};
+  cuuint32_t box[3] = {256, (cuuint32_t)(2 * KBLOCKS), 2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 struct DeviceInfo {
   int sms = 0;
   int max_clusters = 0;
@@ -887,7 +915,7 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   if (!make_map(&ma, a, m, k / 2, BK_BYTES, CTA_M, swz) ||
       !make_map(&mb, b, n, k / 2, BK_BYTES, CTA_N, swz) ||
       !make_map(&msa, sfa, pad_m * sf_atoms * 4 / 256, 256, 256, 2 * KBLOCKS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map(&msb, sfb, pad_n * sf_atoms * 4 / 256, 256, 256, 2 * KBLOCKS, CU_TENSOR_MAP_SWIZZLE_NONE))
+      !make_map_sf_groups(&msb, sfb, pad_n / 128, sf_atoms * 2))
     return NVFP4B200_ERR_CUDA;
   // bf16 output viewed as bytes: [m rows, 2n bytes], row stride 2*ldd, boxes of 32 rows x 128 bytes
   CUtensorMap mh;
