@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define NVFP4B200_API_VERSION 2
+#define NVFP4B200_API_VERSION 3
 
 enum nvfp4b200_status {
   NVFP4B200_OK = 0,
@@ -75,6 +75,17 @@ int nvfp4b200_set_gemm_max_sms(int max_sms);
 int nvfp4b200_gemm_swiglu(const void* a, const void* b, const void* sfa, const void* sfb, const float* scale_a,
                           const float* scale_b, void* h, void* gu, uint32_t* ws, float* h_global_scale_out,
                           int64_t m, int64_t n, int64_t k, void* stream);
+
+/* dh GEMM with the SwiGLU backward in its epilogue (new: the MLP backward; no
+ * counterpart in the reference).  The product dh = scale_a * scale_b * (A . B^T)
+ * ([m, n]) is rounded to bf16 and never stored; gu: bf16 [m, 2n] gate/up
+ * values interleaved in blocks of 128 (nvfp4b200_gemm_swiglu's layout);
+ * dgu: bf16 [m, 2n] in the same layout, exactly nvfp4b200_swiglu_bwd(gu, dh,
+ * interleave = 128).  n % 256 == 0.  ws (2 x u32, zero on entry, left zero)
+ * with dgu_global_scale_out: device global scale of dgu, or both NULL. */
+int nvfp4b200_gemm_dswiglu(const void* a, const void* b, const void* sfa, const void* sfb, const float* scale_a,
+                           const float* scale_b, const void* gu, void* dgu, uint32_t* ws,
+                           float* dgu_global_scale_out, int64_t m, int64_t n, int64_t k, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Quantizers                                                               */

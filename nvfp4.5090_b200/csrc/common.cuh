@@ -59,6 +59,16 @@ __device__ __forceinline__ float e4m3_decode(uint32_t c) {
                 : __uint_as_float(((e + 120u) << 23) | (m << 20));
 }
 
+// SwiGLU backward of one element: gate g, up u, upstream gradient d (all
+// bf16 values), sg = sigmoid(g).  du = d * (g * sg) and
+// dg = (d * u) * (sg * (1 + g * (1 - sg))), every step rounded as written and
+// 1 + g * (1 - sg) one fused multiply-add, so the element-wise kernel and the
+// GEMM epilogue that both use this give identical bits.
+__device__ __forceinline__ void swiglu_grad(float g, float u, float d, float sg, float& dg, float& du) {
+  du = __fmul_rn(d, __fmul_rn(g, sg));
+  dg = __fmul_rn(__fmul_rn(d, u), __fmul_rn(sg, __fmaf_rn(g, __fsub_rn(1.0f, sg), 1.0f)));
+}
+
 // ---------------------------------------------------------------------------
 // packed f32 pairs: one 64-bit register holds two floats and each f32x2
 // instruction performs two independent IEEE single-precision operations,

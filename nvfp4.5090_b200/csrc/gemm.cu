@@ -74,13 +74,20 @@ constexpr int ACC1_COL = 192;                         // buffer 1 starts inside 
 constexpr int SF_COL = 448;                           // scale slot: A 4 x 4 columns, then B 4 x 8 columns
 constexpr int SF_COLS = 12 * KBLOCKS;
 static_assert(ACC1_COL + ACC_COLS <= SF_COL && SF_COL + SF_COLS <= TMEM_COLS, "TMEM columns");
-constexpr int NUM_BARS = 2 * STAGES + 3;           // full, empty, tmem_full, overlap_free, drain
+constexpr int NUM_BARS = 2 * STAGES + 3 + EPI_WARPS;  // full, empty, tmem_full, overlap_free, drain, epilogue loads
 constexpr int BAR_BYTES = 512;                        // mbarriers + TMEM address slot + abort flag
 static_assert(NUM_BARS * 8 + 8 <= BAR_BYTES, "barrier area");
 constexpr int OUT_CHUNK_BYTES = 32 * 128;             // one epilogue warp's 32 rows x 64 bf16 output chunk
 constexpr int OUT_BYTES = EPI_WARPS * OUT_CHUNK_BYTES;  // bf16 output staging for the TMA stores
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024 + BAR_BYTES;  // + worst-case 1 KB alignment
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+// SwiGLU-backward epilogue: one stage fewer, two 4 KB slots per epilogue warp
+// (the gate and up inputs arrive there by TMA; the gradients leave from there).
+constexpr int DSW_STAGES = STAGES - 1;
+constexpr int DSW_SLOT_BYTES = 32 * 128;               // 32 rows x 64 bf16, 128-byte swizzle
+constexpr int DSW_OUT_BYTES = EPI_WARPS * 2 * DSW_SLOT_BYTES;
+constexpr int DSW_SMEM_BYTES = DSW_STAGES * STAGE_BYTES + DSW_OUT_BYTES + 1024 + BAR_BYTES;
+static_assert(DSW_SMEM_BYTES <= SMEM_BYTES, "the launch attribute covers both layouts");
 constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;  // about 2 s at 2 GHz
 constexpr int GROUP_M = 8;                            // raster: 8 pair-rows (2048 rows) per group
 
@@ -101,7 +108,10 @@ struct Params {
   int d_f32, accumulate, epilogue;
   int swiglu;                // B rows interleaved [gate 128 | up 128] per tile: d = silu(gate)*up
   int store_gu;              // swiglu: also store the bf16 gate/up tile (tmap_d)
-  uint32_t* h_amax;          // swiglu: atomic max of |h| (float bits), or null
+  uint32_t* h_amax;          // swiglu / dswiglu: atomic max of |h| or |dgu| (float bits), or null
+  int dswiglu;               // D = dh -> dgu = SwiGLU backward against gate/up (tmap_h loads, tmap_d stores)
+  int stages;                // pipeline stages in use (STAGES, or DSW_STAGES with dswiglu)
+  int out_bytes;             // epilogue staging bytes (OUT_BYTES or DSW_OUT_BYTES)
 };
 
 // ---------------------------------------------------------------------------
@@ -237,6 +247,20 @@ __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.w
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+// 2-D tiled TMA load into this CTA's shared memory, completion on this CTA's barrier.
+__device__ __forceinline__ void tma_load_2d_local(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(map), "r"(bar), "r"(x), "r"(y)
+      : "memory");
 }
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
@@ -388,12 +412,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                       const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int nst = p.stages;
   uint8_t* sA = smem;
-  uint8_t* sB = sA + STAGES * A_BYTES;
-  uint8_t* sSFA = sB + STAGES * B_BYTES;
-  uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
-  uint8_t* sOut = sSFB + STAGES * SFB_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + OUT_BYTES);
+  uint8_t* sB = sA + nst * A_BYTES;
+  uint8_t* sSFA = sB + nst * B_BYTES;
+  uint8_t* sSFB = sSFA + nst * SFA_BYTES;
+  uint8_t* sOut = sSFB + nst * SFB_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + p.out_bytes);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -405,6 +430,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem_full_bar = smem_u32(bars + 2 * STAGES);            // both: a tile's accumulator is final
   const uint32_t overlap_free_bar = smem_u32(bars + 2 * STAGES + 1);     // leader: shared columns drained
   const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 2);            // leader: error-path drain
+  auto load_bar = [&](int w) { return smem_u32(bars + 2 * STAGES + 3 + w); };  // epilogue warp w's TMA loads
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -414,6 +440,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     mbar_init(tmem_full_bar, 1);
     mbar_init(overlap_free_bar, 2 * EPI_WARPS);
     mbar_init(drain_bar, 1);
+    for (int w = 0; w < EPI_WARPS; ++w) mbar_init(load_bar(w), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tmap(&tmap_a);
@@ -421,7 +448,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     prefetch_tmap(&tmap_sfa);
     prefetch_tmap(&tmap_sfb);
     prefetch_tmap(&tmap_d);
-    if (p.swiglu) prefetch_tmap(&tmap_h);
+    if (p.swiglu || p.dswiglu) prefetch_tmap(&tmap_h);
   }
   if (warp == 1) {
     tmem_alloc2(smem_u32(tmem_slot), TMEM_COLS);
@@ -468,7 +495,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         __syncwarp();
         armed |= 1u << stage;
         armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
-        if (++stage == STAGES) {
+        if (++stage == nst) {
           stage = 0;
           phase ^= 1;
         }
@@ -478,7 +505,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       raise_abort(abort_flag);
       if (leader) {  // the leader's stage barriers count both CTAs' copies: let them land
         const long long t0 = clock64();
-        for (int st = 0; st < STAGES; ++st) {
+        for (int st = 0; st < nst; ++st) {
           if (!((armed >> st) & 1u)) continue;
           while (!mbar_try_wait(full_bar(st), (armed_parity >> st) & 1u) && clock64() - t0 < WAIT_LIMIT_CYCLES) {
           }
@@ -528,7 +555,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           }
           __syncwarp();
           issued = true;
-          if (++stage == STAGES) {
+          if (++stage == nst) {
             stage = 0;
             phase ^= 1;
           }
@@ -547,6 +574,135 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+  } else if (p.dswiglu) {
+    // ---------------- SwiGLU-backward epilogue (warps 2..9, both CTAs) ----------------
+    // The accumulator is dh (rounded to bf16 exactly as a stored dh would be);
+    // the gate/up tensor gu [m, 2n] holds [gate 128 | up 128] per 256 columns,
+    // and dgu (same layout) = (dgate, dup) of swiglu_grad.  Warp (quad, half)
+    // owns rows [32 quad, +32) of its CTA's half tile and dh columns
+    // [128 half, +128), i.e. interleave block t = 2 nb + half (gu columns
+    // [256 t, 256 t + 256)).  Per 64-column chunk the warp's two slots receive
+    // the gate and the up values by TMA, are overwritten with the two
+    // gradients and stored.  The next chunk's (or next tile's first chunk's)
+    // loads are issued as soon as the stores have read the slots, so the first
+    // chunk of a tile is in flight while the warp waits for the accumulator.
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int ew = warp - 2;
+    const uint32_t leader_overlap_free = map_to_rank(overlap_free_bar, 0);
+    const float alpha = (p.scale_a ? *p.scale_a : 1.0f) * (p.scale_b ? *p.scale_b : 1.0f);
+    const uint32_t slot_g = smem_u32(sOut + ew * 2 * DSW_SLOT_BYTES);
+    const uint32_t slot_u = slot_g + DSW_SLOT_BYTES;
+    const uint32_t lbar = load_bar(ew);
+    uint32_t ld_par = 0;
+    bool ld_pending = false;
+    uint32_t amax16 = 0;   // max |dgu| as bf16 magnitude bits (NaN ignored)
+    auto issue_loads = [&](int mb_, int nb_, int c) {
+      const int y = mb_ * TILE_M + (int)rank * CTA_M + quad * 32;
+      const int gcol = 256 * (2 * nb_ + half) + 64 * c;   // gate column of the chunk (elements)
+      if (elect_one()) {
+        mbar_expect_tx(lbar, 2 * DSW_SLOT_BYTES);
+        tma_load_2d_local(slot_g, &tmap_h, lbar, 2 * gcol, y);          // x in bytes
+        tma_load_2d_local(slot_u, &tmap_h, lbar, 2 * (gcol + 128), y);
+      }
+      __syncwarp();
+      ld_pending = true;
+    };
+    bool ok = true;
+    int it = 0;
+    if (cluster_id < total_tiles) {
+      int mb0, nb0;
+      tile_coords(cluster_id, p, mb0, nb0);
+      issue_loads(mb0, nb0, half == 1 ? 1 : 0);   // tile 0 uses buffer 0: half 1 drains chunk 1 first
+    }
+    for (int tile = cluster_id; tile < total_tiles; tile += num_clusters, ++it) {
+      int mb, nb;
+      tile_coords(tile, p, mb, nb);
+      ok = __all_sync(0xffffffffu, mbar_wait(tmem_full_bar, (uint32_t)(it & 1), abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const int buf = it & 1;
+      const int first = (buf == 0 && half == 1) ? 1 : 0;   // the chunk in the columns both buffers share
+      const int y0 = mb * TILE_M + (int)rank * CTA_M + quad * 32;
+      const bool row_ok = y0 + lane < p.m;
+      const uint32_t tbase =
+          tmem_base + (buf ? ACC1_COL : 0) + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * 128);
+      const uint32_t orow_g = slot_g + lane * 128, orow_u = slot_u + lane * 128;
+      for (int r = 0; r < 2; ++r) {
+        const int c = r ^ first;
+        uint32_t acc[64];
+        __syncwarp();
+        tmem_ld32(tbase + c * 64, acc);
+        tmem_ld32(tbase + c * 64 + 32, acc + 32);
+        tmem_ld_wait();
+        if (r == 0) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(leader_overlap_free);
+        }
+        ok = warp_wait(lbar, ld_par, abort_flag);
+        if (!ok) break;   // the load stays pending: waited for (bounded) before exit
+        ld_par ^= 1u;
+        ld_pending = false;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t off = (uint32_t)((j ^ (lane & 7)) << 4);
+          const uint4 gv = ld_shared_v4(orow_g + off);
+          const uint4 uv = ld_shared_v4(orow_u + off);
+          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+          uint32_t og[4], ou[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = 8 * j + 2 * e;
+            const uint32_t dw = pack_bf16x2(__uint_as_float(acc[i]) * alpha, __uint_as_float(acc[i + 1]) * alpha);
+            float dg0, du0, dg1, du1;
+            const float g0 = bf16lo(gw[e]), g1 = bf16hi(gw[e]);
+            swiglu_grad(g0, bf16lo(uw[e]), bf16lo(dw), silu_sigmoid(g0), dg0, du0);
+            swiglu_grad(g1, bf16hi(uw[e]), bf16hi(dw), silu_sigmoid(g1), dg1, du1);
+            og[e] = pack_bf16x2(dg0, dg1);
+            ou[e] = pack_bf16x2(du0, du1);
+            uint32_t a = og[e] & 0x7FFF7FFFu, b = ou[e] & 0x7FFF7FFFu;
+            a &= ~__vcmpgtu2(a, 0x7F807F80u);
+            b &= ~__vcmpgtu2(b, 0x7F807F80u);
+            if (row_ok) amax16 = max(amax16, max(max(a & 0xFFFFu, a >> 16), max(b & 0xFFFFu, b >> 16)));
+          }
+          st_shared_v4(orow_g + off, og[0], og[1], og[2], og[3]);
+          st_shared_v4(orow_u + off, ou[0], ou[1], ou[2], ou[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        const int gcol = 256 * (2 * nb + half) + 64 * c;
+        if (lane == 0 && y0 < p.m) {
+          tma_store_2d(&tmap_d, slot_g, 2 * gcol, y0);
+          tma_store_2d(&tmap_d, slot_u, 2 * (gcol + 128), y0);
+          bulk_commit();
+        }
+        if (lane == 0) bulk_wait_read();   // the slots are free again
+        __syncwarp();
+        if (r == 0) {
+          issue_loads(mb, nb, c ^ 1);
+        } else if (tile + num_clusters < total_tiles) {
+          int mb2, nb2;
+          tile_coords(tile + num_clusters, p, mb2, nb2);
+          issue_loads(mb2, nb2, (((it + 1) & 1) == 0 && half == 1) ? 1 : 0);
+        }
+      }
+      if (!ok) break;
+    }
+    if (!ok && lane == 0) raise_abort(abort_flag);
+    if (ld_pending) {   // a load still in flight lands before the CTA exits
+      if (lane == 0) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(lbar, ld_par) && clock64() - t0 < WAIT_LIMIT_CYCLES) {
+        }
+      }
+      __syncwarp();
+    }
+    if (p.h_amax) {
+      amax16 = __reduce_max_sync(0xffffffffu, amax16);
+      if (lane == 0 && amax16) atomicMax(p.h_amax, amax16 << 16);
+    }
+    if (lane == 0) bulk_wait_all();
   } else {
     // ---------------- epilogue (warps 2..9, both CTAs) ----------------
     const int quad = warp & 3;               // TMEM lanes [32*quad, 32*quad+32)
@@ -888,10 +1044,18 @@ __global__ void h_scale_finalize_kernel(uint32_t* ws, float* g_out) {
   ws[0] = 0u;
 }
 
+// SwiGLU backward in the epilogue: gate/up input [m, 2n] (interleaved blocks of
+// 128), d is the dgu output [m, 2n]; optional global scale of dgu.
+struct DswigluIn {
+  const void* gu;
+  uint32_t* ws;
+  float* g_out;
+};
+
 static int run(const void* a, const void* b, const void* sfa, const void* sfb, const float* scale_a,
                const float* scale_b, const void* bias, const void* residual, void* d, int d_dtype, int accumulate,
                int epilogue, int64_t m, int64_t n, int64_t k, int64_t ldd, cudaStream_t stream,
-               const SwigluOut* sw = nullptr) {
+               const SwigluOut* sw = nullptr, const DswigluIn* dsw = nullptr) {
   if (!a || !b || !sfa || !sfb || !d) return NVFP4B200_ERR_INVALID_ARG;
   if (d_dtype != NVFP4B200_BF16 && d_dtype != NVFP4B200_F32) return NVFP4B200_ERR_INVALID_ARG;
   if (epilogue < 0 || epilogue > 2) return NVFP4B200_ERR_INVALID_ARG;
@@ -920,7 +1084,12 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   // bf16 output viewed as bytes: [m rows, 2n bytes], row stride 2*ldd, boxes of 32 rows x 128 bytes
   CUtensorMap mh;
   memset(&mh, 0, sizeof(mh));
-  if (sw) {
+  if (dsw) {
+    // gate/up input and dgu output, both bf16 [m, 2n] viewed as bytes
+    if (!make_map(&mh, dsw->gu, m, 4 * n, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B, 4 * n) ||
+        !make_map(&md, d, m, 4 * n, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B, 4 * n))
+      return NVFP4B200_ERR_CUDA;
+  } else if (sw) {
     // h [m, n/2] and the optional gate/up [m, n], both bf16 viewed as bytes
     if (!make_map(&mh, d, m, n, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B, n)) return NVFP4B200_ERR_CUDA;
     if (sw->gu && !make_map(&md, sw->gu, m, 2 * n, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B, 2 * n))
@@ -949,7 +1118,11 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   p.epilogue = epilogue;
   p.swiglu = sw ? 1 : 0;
   p.store_gu = (sw && sw->gu) ? 1 : 0;
-  p.h_amax = sw ? sw->ws : nullptr;
+  p.h_amax = sw ? sw->ws : (dsw ? dsw->ws : nullptr);
+  p.dswiglu = dsw ? 1 : 0;
+  p.stages = dsw ? DSW_STAGES : STAGES;
+  p.out_bytes = dsw ? DSW_OUT_BYTES : OUT_BYTES;
+  const int smem_bytes = dsw ? DSW_SMEM_BYTES : SMEM_BYTES;
   const int64_t tiles = (int64_t)p.num_m_tiles * p.num_n_tiles;
   const DeviceInfo info = device_info();
   int cap = info.max_clusters;
@@ -959,11 +1132,12 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   if (cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
       cudaSuccess)
     return NVFP4B200_ERR_CUDA;
-  nvfp4_gemm_kernel<<<2 * clusters, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, msa, msb, md, mh, p);
-  if (sw && sw->ws) {
+  nvfp4_gemm_kernel<<<2 * clusters, NUM_THREADS, smem_bytes, stream>>>(ma, mb, msa, msb, md, mh, p);
+  uint32_t* ws = sw ? sw->ws : (dsw ? dsw->ws : nullptr);
+  if (ws) {
     const int lrc = launch_status();
     if (lrc) return lrc;
-    h_scale_finalize_kernel<<<1, 1, 0, stream>>>(sw->ws, sw->g_out);
+    h_scale_finalize_kernel<<<1, 1, 0, stream>>>(ws, sw ? sw->g_out : dsw->g_out);
   }
   return launch_status();
 }
@@ -1011,6 +1185,17 @@ int nvfp4b200_gemm_swiglu(const void* a, const void* b, const void* sfa, const v
   gemm::SwigluOut sw{gu, ws, h_global_scale_out};
   return gemm::run(a, b, sfa, sfb, scale_a, scale_b, nullptr, nullptr, h, NVFP4B200_BF16, 0, NVFP4B200_EPI_NONE, m, n,
                    k, n, (cudaStream_t)stream, &sw);
+}
+
+int nvfp4b200_gemm_dswiglu(const void* a, const void* b, const void* sfa, const void* sfb, const float* scale_a,
+                           const float* scale_b, const void* gu, void* dgu, uint32_t* ws, float* dgu_global_scale_out,
+                           int64_t m, int64_t n, int64_t k, void* stream) {
+  if (!gu || !dgu || (ws == nullptr) != (dgu_global_scale_out == nullptr)) return NVFP4B200_ERR_INVALID_ARG;
+  if (n <= 0 || n % gemm::TILE_N) return NVFP4B200_ERR_BAD_SHAPE;   // whole 256-column dh tiles
+  if (!aligned(gu, 16) || (ws && !aligned(ws, 4))) return NVFP4B200_ERR_MISALIGNED;
+  gemm::DswigluIn dsw{gu, ws, dgu_global_scale_out};
+  return gemm::run(a, b, sfa, sfb, scale_a, scale_b, nullptr, nullptr, dgu, NVFP4B200_BF16, 0, NVFP4B200_EPI_NONE, m,
+                   n, k, n, (cudaStream_t)stream, nullptr, &dsw);
 }
 
 int nvfp4b200_nvfp4_mm(const void* a, const void* b, const void* sfa, const void* sfb, const float* output_scale,

@@ -102,9 +102,7 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint16_t* __restr
           const float g = e ? bf16hi(gw[j]) : bf16lo(gw[j]);
           const float u = e ? bf16hi(uw[j]) : bf16lo(uw[j]);
           const float d = e ? bf16hi(dw[j]) : bf16lo(dw[j]);
-          const float sg = sigmoidf_(g);
-          du[e] = d * (g * sg);
-          dg[e] = d * u * (sg * (1.0f + g * (1.0f - sg)));
+          swiglu_grad(g, u, d, sigmoidf_(g), dg[e], du[e]);
         }
         og[j] = pack2(dg[0], dg[1]);
         ou[j] = pack2(du[0], du[1]);

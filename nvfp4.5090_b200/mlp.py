@@ -27,8 +27,11 @@ W_gu's 2F rows may be stored [W_gate; W_up] (``interleave=0``) or with gate
 and up rows alternating in blocks of 128 (``interleave=128``).  The latter
 lets the gate/up GEMM apply SwiGLU in its epilogue (each 256-column output
 tile holds 128 gate columns and their up columns), so h and its global
-scale come out of that GEMM; every other GEMM only sees a relabelled 2F
-dimension.  NVFP4MLPStackTrainer keeps W_gu interleaved.
+scale come out of that GEMM, and the dh GEMM to apply the SwiGLU backward
+in its epilogue (each 256-column dh tile meets two whole gate/up blocks;
+F % 256 == 0), so dgu and its global scale come out of that GEMM and dh is
+never stored.  Every other GEMM only sees a relabelled 2F dimension.
+NVFP4MLPStackTrainer keeps W_gu interleaved.
 """
 from __future__ import annotations
 
@@ -112,15 +115,22 @@ def block_backward(dy: torch.Tensor, gamma: torch.Tensor, qw: QWeights, sv: Save
     Returns dx [T, D] (including the residual path)."""
     g_dy = ops.global_scale(dy)
     q_dy, s_dy = ops.quantize(dy, global_scale=g_dy)
-    dh = ops.gemm(q_dy, s_dy, qw.q_down_t, qw.s_down_t, scale_a=g_dy, scale_b=qw.g_down)
+    # interleaved gate/up with whole 256-column dh tiles: the SwiGLU backward
+    # runs in the dh GEMM's epilogue and dh is never stored
+    fused = interleave == 128 and (sv.gu.shape[1] // 2) % 256 == 0
+    if fused:
+        dgu, g_dgu = ops.gemm_dswiglu(q_dy, s_dy, qw.q_down_t, qw.s_down_t, sv.gu, scale_a=g_dy, scale_b=qw.g_down)
+    else:
+        dh = ops.gemm(q_dy, s_dy, qw.q_down_t, qw.s_down_t, scale_a=g_dy, scale_b=qw.g_down)
     del q_dy, s_dy
     # wgrad of W_down: dy^T . h  (contraction over tokens)
     q_dyt, s_dyt = ops.quantize_t(dy, global_scale=g_dy)
     q_ht, s_ht = ops.quantize_t(sv.h, global_scale=sv.g_h)
     ops.gemm(q_dyt, s_dyt, q_ht, s_ht, scale_a=g_dy, scale_b=sv.g_h, out=grad_down, accumulate=accumulate)
     del q_dyt, s_dyt, q_ht, s_ht
-    dgu, g_dgu = ops.swiglu_bwd(sv.gu, dh, with_scale=True, interleave=interleave)
-    del dh
+    if not fused:
+        dgu, g_dgu = ops.swiglu_bwd(sv.gu, dh, with_scale=True, interleave=interleave)
+        del dh
     q_dgu, s_dgu = ops.quantize(dgu, global_scale=g_dgu)
     dxn = ops.gemm(q_dgu, s_dgu, qw.q_gu_t, qw.s_gu_t, scale_a=g_dgu, scale_b=qw.g_gu)
     del q_dgu, s_dgu

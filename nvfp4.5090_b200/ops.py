@@ -273,6 +273,33 @@ def gemm_swiglu(qa: torch.Tensor, sa: torch.Tensor, qb: torch.Tensor, sb: torch.
     return h, gu, g
 
 
+def gemm_dswiglu(qa: torch.Tensor, sa: torch.Tensor, qb: torch.Tensor, sb: torch.Tensor, gu: torch.Tensor, *,
+                 scale_a: Optional[torch.Tensor] = None, scale_b: Optional[torch.Tensor] = None,
+                 with_scale: bool = True):
+    """dh GEMM (A = dy [m, k], B = W_down^T [n, k]) with the SwiGLU backward in
+    the epilogue against gu [m, 2n] (gate/up interleaved in blocks of 128).
+    Returns (dgu bf16 [m, 2n], g(dgu) or None); dh itself is not stored."""
+    _require(qa.is_cuda and qb.is_cuda and gu.is_cuda, "gemm_dswiglu requires CUDA tensors")
+    m, kh = qa.shape
+    n, kh2 = qb.shape
+    _require(kh == kh2, f"K mismatch: A has {2 * kh}, B has {2 * kh2}")
+    _require(n % 256 == 0, "gemm_dswiglu needs n (= F) % 256 == 0")
+    _check_bf16(gu, "gu")
+    _require(tuple(gu.shape) == (m, 2 * n) and gu.is_contiguous(), "gu must be contiguous bf16 [m, 2n]")
+    k = 2 * kh
+    _require(qa.is_contiguous() and qb.is_contiguous() and sa.is_contiguous() and sb.is_contiguous(),
+             "gemm operands must be contiguous")
+    _require(sa.numel() == math.prod(scale_shape(m, k)) and sb.numel() == math.prod(scale_shape(n, k)),
+             "scale tensors must be the padded swizzled [round_up(rows,128), round_up(k/16,4)] layout")
+    dgu = torch.empty((m, 2 * n), device=qa.device, dtype=torch.bfloat16)
+    g = torch.empty((1,), device=qa.device, dtype=torch.float32) if with_scale else None
+    ws = workspace(qa.device) if with_scale else None
+    _lib.call("nvfp4b200_gemm_dswiglu", qa.data_ptr(), qb.data_ptr(), sa.data_ptr(), sb.data_ptr(),
+              _ptr(_scalar_f32(scale_a, qa.device)), _ptr(_scalar_f32(scale_b, qa.device)), gu.data_ptr(),
+              dgu.data_ptr(), _ptr(ws), _ptr(g), m, n, k, _stream(qa))
+    return dgu, g
+
+
 def rmsnorm_bwd(x: torch.Tensor, gamma: Optional[torch.Tensor], inv_rms: torch.Tensor, dy: torch.Tensor,
                 dres: Optional[torch.Tensor] = None, dgamma_acc: Optional[torch.Tensor] = None) -> torch.Tensor:
     r, k = x.shape

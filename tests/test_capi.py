@@ -68,6 +68,14 @@ MIS = FAKE + 4
                                        None), 2),                                         # n % 256
     (lambda L: L.nvfp4b200_gemm_swiglu(FAKE, FAKE, FAKE, FAKE, None, None, FAKE, None, FAKE, None, 8, 512, 64,
                                        None), 1),                                         # ws without g_out
+    (lambda L: L.nvfp4b200_gemm_dswiglu(FAKE, FAKE, FAKE, FAKE, None, None, FAKE, FAKE, None, None, 8, 384, 64,
+                                        None), 2),                                        # n % 256
+    (lambda L: L.nvfp4b200_gemm_dswiglu(FAKE, FAKE, FAKE, FAKE, None, None, None, FAKE, None, None, 8, 512, 64,
+                                        None), 1),                                        # no gate/up input
+    (lambda L: L.nvfp4b200_gemm_dswiglu(FAKE, FAKE, FAKE, FAKE, None, None, MIS, FAKE, None, None, 8, 512, 64,
+                                        None), 3),                                        # misaligned gate/up
+    (lambda L: L.nvfp4b200_gemm_dswiglu(FAKE, FAKE, FAKE, FAKE, None, None, FAKE, FAKE, None, FAKE, 8, 512, 64,
+                                        None), 1),                                        # g_out without ws
     (lambda L: L.nvfp4b200_adamw_step(FAKE, FAKE, 5, FAKE, FAKE, 8, 1e-3, .9, .95, 1e-8, 0., 1., 1., 1., None), 1),
 ])
 def test_argument_validation_without_device(pkg, call, expected):

@@ -168,6 +168,34 @@ def test_gemm_swiglu_equals_gemm_then_swiglu(pkg):
     assert gu2 is None and g2 is None and torch.equal(h2.view(torch.int16), h_ref.view(torch.int16))
 
 
+@pytest.mark.parametrize("m,n,k,max_sms", [(300, 512, 384, 0), (2048, 2560, 512, 0), (700, 1024, 256, 8)])
+def test_gemm_dswiglu_equals_gemm_then_swiglu_bwd(pkg, m, n, k, max_sms):
+    """The SwiGLU-backward epilogue gives bit-identical dgu and global scale to
+    the plain dh GEMM followed by the element-wise SwiGLU backward (ragged M,
+    a partial last K tile, and clusters that walk many tiles when the GEMM is
+    capped to 8 SMs)."""
+    gen = torch.Generator(device="cuda").manual_seed(m + n + k)
+    dy = (1e-3 * torch.randn(m, k, device="cuda", generator=gen)).to(torch.bfloat16)
+    wdt = (0.05 * torch.randn(n, k, device="cuda", generator=gen)).to(torch.bfloat16)
+    gu = (2 * torch.randn(m, 2 * n, device="cuda", generator=gen)).to(torch.bfloat16)
+    ga, gw = pkg.ops.global_scale(dy), pkg.ops.global_scale(wdt)
+    qa, sa = pkg.ops.quantize(dy, global_scale=ga)
+    qw, sw = pkg.ops.quantize(wdt, global_scale=gw)
+    try:
+        pkg.ops.set_gemm_max_sms(max_sms)
+        dgu, g = pkg.ops.gemm_dswiglu(qa, sa, qw, sw, gu, scale_a=ga, scale_b=gw)
+        dh = pkg.ops.gemm(qa, sa, qw, sw, scale_a=ga, scale_b=gw)
+    finally:
+        pkg.ops.set_gemm_max_sms(0)
+    dgu_ref, g_ref = pkg.ops.swiglu_bwd(gu, dh, with_scale=True, interleave=128)
+    torch.cuda.synchronize()
+    assert pkg.ops.device_error() == 0
+    assert torch.equal(dgu.view(torch.int16), dgu_ref.view(torch.int16))
+    assert torch.equal(g, g_ref)
+    dgu2, g2 = pkg.ops.gemm_dswiglu(qa, sa, qw, sw, gu, scale_a=ga, scale_b=gw, with_scale=False)
+    assert g2 is None and torch.equal(dgu2.view(torch.int16), dgu_ref.view(torch.int16))
+
+
 def test_swiglu_interleaved_layout_equals_halves(pkg):
     t, f = 96, 256
     gen = torch.Generator(device="cuda").manual_seed(12)
