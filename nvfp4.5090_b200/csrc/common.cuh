@@ -92,8 +92,21 @@ __device__ __forceinline__ uint64_t f2mul_plus_zero(uint64_t a, uint64_t b) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(0ull));
   return r;
 }
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
 // bf16 pair word -> {lo, hi} as a packed f32 pair, exactly
 __device__ __forceinline__ uint64_t bf16x2_to_f2(uint32_t w) { return f2pack(bf16lo(w), bf16hi(w)); }
+// swiglu_grad on two elements at once (per lane the same roundings; 1 - sg
+// as fma(sg, -1, 1), one rounding of the exact difference like the subtraction)
+__device__ __forceinline__ void swiglu_grad2(uint64_t g, uint64_t u, uint64_t d, uint64_t sg, uint64_t& dg,
+                                             uint64_t& du) {
+  const uint64_t one = f2pack(1.0f, 1.0f), neg1 = f2pack(-1.0f, -1.0f);
+  du = f2mul(d, f2mul(g, sg));
+  dg = f2mul(f2mul(d, u), f2mul(sg, f2fma(g, f2fma(sg, neg1, one), one)));
+}
 
 // encode8_pairs: 8 values (4 packed pairs) -> 8 E2M1 nibbles (low nibble = even element,
 // float4utils.py:141), each nibble equal to the reference's comparison ladder

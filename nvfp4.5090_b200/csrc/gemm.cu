@@ -591,12 +591,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const int ew = warp - 2;
     const uint32_t leader_overlap_free = map_to_rank(overlap_free_bar, 0);
     const float alpha = (p.scale_a ? *p.scale_a : 1.0f) * (p.scale_b ? *p.scale_b : 1.0f);
+    const uint64_t alpha2 = f2pack(alpha, alpha);
     const uint32_t slot_g = smem_u32(sOut + ew * 2 * DSW_SLOT_BYTES);
     const uint32_t slot_u = slot_g + DSW_SLOT_BYTES;
     const uint32_t lbar = load_bar(ew);
     uint32_t ld_par = 0;
     bool ld_pending = false;
-    uint32_t amax16 = 0;   // max |dgu| as bf16 magnitude bits (NaN ignored)
+    // max |dgu| over this warp's rows, taken on the fp32 values before rounding
+    // (round-to-nearest is monotonic, so bf16(max |x|) = max |bf16(x)|; fmaxf
+    // skips NaN like the element-wise kernels' amax)
+    float amax = 0.0f;
     auto issue_loads = [&](int mb_, int nb_, int c) {
       const int y = mb_ * TILE_M + (int)rank * CTA_M + quad * 32;
       const int gcol = 256 * (2 * nb_ + half) + 64 * c;   // gate column of the chunk (elements)
@@ -644,30 +648,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         if (!ok) break;   // the load stays pending: waited for (bounded) before exit
         ld_par ^= 1u;
         ld_pending = false;
+        // two 32-column halves: all shared loads of a half first, then its 16
+        // independent element pairs, then its stores (a load after a store
+        // cannot move up, so interleaving them would serialise the pairs)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t off = (uint32_t)((j ^ (lane & 7)) << 4);
-          const uint4 gv = ld_shared_v4(orow_g + off);
-          const uint4 uv = ld_shared_v4(orow_u + off);
-          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
-          uint32_t og[4], ou[4];
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t gw[16], uw[16];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = 8 * j + 2 * e;
-            const uint32_t dw = pack_bf16x2(__uint_as_float(acc[i]) * alpha, __uint_as_float(acc[i + 1]) * alpha);
-            float dg0, du0, dg1, du1;
-            const float g0 = bf16lo(gw[e]), g1 = bf16hi(gw[e]);
-            swiglu_grad(g0, bf16lo(uw[e]), bf16lo(dw), silu_sigmoid(g0), dg0, du0);
-            swiglu_grad(g1, bf16hi(uw[e]), bf16hi(dw), silu_sigmoid(g1), dg1, du1);
-            og[e] = pack_bf16x2(dg0, dg1);
-            ou[e] = pack_bf16x2(du0, du1);
-            uint32_t a = og[e] & 0x7FFF7FFFu, b = ou[e] & 0x7FFF7FFFu;
-            a &= ~__vcmpgtu2(a, 0x7F807F80u);
-            b &= ~__vcmpgtu2(b, 0x7F807F80u);
-            if (row_ok) amax16 = max(amax16, max(max(a & 0xFFFFu, a >> 16), max(b & 0xFFFFu, b >> 16)));
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t off = (uint32_t)(((4 * hh + q) ^ (lane & 7)) << 4);
+            const uint4 gv = ld_shared_v4(orow_g + off);
+            const uint4 uv = ld_shared_v4(orow_u + off);
+            gw[4 * q] = gv.x; gw[4 * q + 1] = gv.y; gw[4 * q + 2] = gv.z; gw[4 * q + 3] = gv.w;
+            uw[4 * q] = uv.x; uw[4 * q + 1] = uv.y; uw[4 * q + 2] = uv.z; uw[4 * q + 3] = uv.w;
           }
-          st_shared_v4(orow_g + off, og[0], og[1], og[2], og[3]);
-          st_shared_v4(orow_u + off, ou[0], ou[1], ou[2], ou[3]);
+          uint32_t og[16], ou[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int i = 32 * hh + 2 * e;
+            const uint64_t dh2 = f2mul(f2pack(__uint_as_float(acc[i]), __uint_as_float(acc[i + 1])), alpha2);
+            const uint32_t dw = pack_bf16x2(f2lo(dh2), f2hi(dh2));   // dh as a stored bf16 dh
+            const uint64_t g2 = bf16x2_to_f2(gw[e]);
+            const uint64_t sg2 = f2pack(silu_sigmoid(f2lo(g2)), silu_sigmoid(f2hi(g2)));
+            uint64_t dg2, du2;
+            swiglu_grad2(g2, bf16x2_to_f2(uw[e]), bf16x2_to_f2(dw), sg2, dg2, du2);
+            og[e] = pack_bf16x2(f2lo(dg2), f2hi(dg2));
+            ou[e] = pack_bf16x2(f2lo(du2), f2hi(du2));
+            if (row_ok)
+              amax = fmaxf(fmaxf(amax, fmaxf(fabsf(f2lo(dg2)), fabsf(f2hi(dg2)))),
+                           fmaxf(fabsf(f2lo(du2)), fabsf(f2hi(du2))));
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t off = (uint32_t)(((4 * hh + q) ^ (lane & 7)) << 4);
+            st_shared_v4(orow_g + off, og[4 * q], og[4 * q + 1], og[4 * q + 2], og[4 * q + 3]);
+            st_shared_v4(orow_u + off, ou[4 * q], ou[4 * q + 1], ou[4 * q + 2], ou[4 * q + 3]);
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -699,8 +715,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
     }
     if (p.h_amax) {
-      amax16 = __reduce_max_sync(0xffffffffu, amax16);
-      if (lane == 0 && amax16) atomicMax(p.h_amax, amax16 << 16);
+      const uint32_t a16 = __reduce_max_sync(0xffffffffu, pack_bf16x2(amax, 0.0f) & 0xFFFFu);
+      if (lane == 0 && a16) atomicMax(p.h_amax, a16 << 16);
     }
     if (lane == 0) bulk_wait_all();
   } else {
@@ -777,7 +793,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           }
         }
         uint32_t hw[32];   // h as packed bf16 pairs (64 values)
-        uint32_t hmax = 0;
+        float hmax = 0.0f;  // max |h| before rounding: bf16(max |h|) = max |bf16(h)| (NaN skipped)
 #pragma unroll
         for (int pp = 0; pp < 2; ++pp) {
           uint32_t sr[32];
@@ -798,11 +814,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
               const float f0 = __uint_as_float(fr[32 * pp + i]), f1 = __uint_as_float(fr[32 * pp + i + 1]);
               const float g0 = up_first ? s0 : f0, g1 = up_first ? s1 : f1;
               const float u0 = up_first ? f0 : s0, u1 = up_first ? f1 : s1;
-              const uint32_t hv = pack_bf16x2(g0 * silu_sigmoid(g0) * u0, g1 * silu_sigmoid(g1) * u1);
-              hw[16 * pp + 4 * j + e] = hv;
-              uint32_t a = hv & 0x7FFF7FFFu;
-              a &= ~__vcmpgtu2(a, 0x7F807F80u);
-              hmax = max(hmax, max(a & 0xFFFFu, a >> 16));
+              const float h0 = g0 * silu_sigmoid(g0) * u0, h1 = g1 * silu_sigmoid(g1) * u1;
+              hw[16 * pp + 4 * j + e] = pack_bf16x2(h0, h1);
+              hmax = fmaxf(hmax, fmaxf(fabsf(h0), fabsf(h1)));
             }
             if (p.store_gu) st_shared_v4(orow + (((4 * pp + j) ^ (lane & 7)) << 4), w[0], w[1], w[2], w[3]);
           }
@@ -828,8 +842,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           bulk_commit();
         }
         if (p.h_amax) {
-          hmax = __reduce_max_sync(0xffffffffu, row_ok ? hmax : 0u);
-          if (lane == 0 && hmax) atomicMax(p.h_amax, hmax << 16);
+          const uint32_t h16 = __reduce_max_sync(0xffffffffu, row_ok ? (pack_bf16x2(hmax, 0.0f) & 0xFFFFu) : 0u);
+          if (lane == 0 && h16) atomicMax(p.h_amax, h16 << 16);
         }
       } else if (!p.d_f32) {
         // bf16: each 32-row x 64-column chunk goes through this warp's shared
