@@ -456,9 +456,59 @@ def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=No
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / max(1, args.steps // 2)
     res["e2e"] = {"value": global_tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
                   "h2d_bytes_per_step": 2 * x.numel() * 2 * world, "d2h_bytes_per_step": 4 * world}
+    if getattr(args, "breakdown", False) and world == 1:
+        res["kernel_breakdown"] = step_breakdown(trainer, x, dy, n_blocks, d, f, micro_tokens)
     del trainer
     torch.cuda.empty_cache()
     return res
+
+
+def step_breakdown(trainer, x, dy, n_blocks, d, f, micro):
+    """One extra training step under torch.profiler (CUPTI kernel records, the
+    real overlap, outside every timed region): device time per kernel, and each
+    NVFP4 GEMM launch attributed to its role by its place in the step's fixed
+    launch order (per micro-batch: gate/up and down per block forward, then dh,
+    dW_down, dxn and dW_gu per block backward)."""
+    import collections
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        trainer.step(x, dy)
+        trainer.finish()
+        torch.cuda.synchronize()
+    ks = sorted((e.time_range.start, e.time_range.end, e.name) for e in prof.events()
+                if e.device_type == torch.autograd.DeviceType.CUDA)
+    if not ks:
+        return {"error": "no kernel records"}
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for a, b, n in ks:
+        key = n.split("(")[0]
+        agg[key][0] += 1
+        agg[key][1] += (b - a) / 1e3
+    gem = [(b - a) / 1e3 for a, b, n in ks if "nvfp4_gemm_kernel" in n]
+    per_micro = 6 * n_blocks
+    t = micro
+    flop = {"fwd_gate_up_swiglu": 2 * t * 2 * f * d, "fwd_down": 2 * t * d * f, "bwd_dh_swiglu": 2 * t * f * d,
+            "wgrad_down": 2 * d * f * t, "bwd_dxn": 2 * t * d * 2 * f, "wgrad_gate_up": 2 * 2 * f * d * t}
+    roles = collections.defaultdict(list)
+    for i, ms in enumerate(gem):
+        j = i % per_micro
+        if j < 2 * n_blocks:
+            r = "fwd_gate_up_swiglu" if j % 2 == 0 else "fwd_down"
+        else:
+            r = ["bwd_dh_swiglu", "wgrad_down", "bwd_dxn", "wgrad_gate_up"][(j - 2 * n_blocks) % 4]
+        roles[r].append(ms)
+    busy = sum(v[1] for v in agg.values())
+    span = (ks[-1][1] - ks[0][0]) / 1e3
+    return {
+        "span_ms": span, "kernel_busy_ms": busy, "launches": len(ks),
+        "kernels": [{"name": k, "launches": c, "ms": round(ms, 3), "share": round(ms / busy, 4)}
+                    for k, (c, ms) in sorted(agg.items(), key=lambda kv: -kv[1][1])[:16]],
+        "gemm_roles": {r: {"launches": len(v), "mean_ms": round(sum(v) / len(v), 4),
+                           "tflops": round(flop[r] / (sum(v) / len(v) * 1e-3) / 1e12, 1)} for r, v in roles.items()},
+        "note": "one step under torch.profiler (CUPTI), after the timed steps; per-kernel device time with real overlap",
+    }
 
 
 # ---------------------------------------------------------------------------
@@ -524,6 +574,8 @@ def main(argv=None):
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the GEMM M sweep")
     ap.add_argument("--no-clock-hold", action="store_true", help="skip the 1 s sustained clock window (profiling)")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="after the timed MLP steps, one more step under torch.profiler: per-kernel device time")
     ap.add_argument("--only", choices=["gemm", "quant", "mlp_block", "mlp_stack"], default=None,
                     help="run one section and print its result (profiling runs)")
     args = ap.parse_args(argv)

@@ -62,6 +62,13 @@ int nvfp4b200_get_device_error(int* out);
  * NVFP4B200_ERR_INVALID_ARG for negative values. */
 int nvfp4b200_set_gemm_max_sms(int max_sms);
 
+/* Failure-path self-test (no reference counterpart): one warp runs the GEMM
+ * pipeline's bounded mbarrier wait on a barrier that nothing arrives on.
+ * After limit_cycles SM cycles (1 .. 2^32) the wait gives up, the kernel
+ * records NVFP4B200_ERR_TIMEOUT in the device error word (read and cleared by
+ * nvfp4b200_get_device_error) and returns; the context stays usable. */
+int nvfp4b200_wait_selftest(int64_t limit_cycles, void* stream);
+
 /* Gate/up GEMM with the SwiGLU activation in its epilogue (new: the MLP
  * forward; no counterpart in the reference).  b: [n, k/2] packed, whose rows
  * interleave gate and up weights in blocks of 128 (rows 256 t .. 256 t + 127

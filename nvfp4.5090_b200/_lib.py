@@ -24,6 +24,7 @@ SIGNATURES = {
     "nvfp4b200_device_check": [],
     "nvfp4b200_get_device_error": [ctypes.POINTER(c_int)],
     "nvfp4b200_set_gemm_max_sms": [c_int],
+    "nvfp4b200_wait_selftest": [c_i64, c_void_p],
     "nvfp4b200_quant_nvfp4": [c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_void_p, c_void_p],
     "nvfp4b200_scaled_quant_nvfp4": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_void_p,
                                      c_void_p],

@@ -168,7 +168,8 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 // Bounded wait for the phase with the given parity to complete.  Returns
 // false when the CTA-wide abort flag is raised or the limit expires.
 template <bool CLUSTER = false>
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          long long limit_cycles = WAIT_LIMIT_CYCLES) {
   auto try_once = [&]() { return CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity); };
   if (try_once()) return true;
   const long long t0 = clock64();
@@ -176,7 +177,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     if (try_once()) return true;
     if ((it & 63) == 0) {
       if (*abort_flag) return false;
-      if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+      if (clock64() - t0 > limit_cycles) return false;
     }
   }
 }
@@ -1052,6 +1053,22 @@ struct SwigluOut {
 };
 
 // g = amax / 2688 from the amax bits in ws[0] (1 when 0 or not finite); resets ws[0].
+// Failure-path self-test: one warp waits, through the pipeline's bounded wait,
+// for a barrier phase that nothing completes; the wait gives up after
+// limit_cycles, records NVFP4B200_ERR_TIMEOUT and the kernel returns.
+__global__ void wait_selftest_kernel(long long limit_cycles) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bar), 0, &abort_flag, limit_cycles));
+  if (!ok && threadIdx.x == 0) raise_abort(&abort_flag);
+}
+
 __global__ void h_scale_finalize_kernel(uint32_t* ws, float* g_out) {
   const float amax = __uint_as_float(ws[0]);
   *g_out = (amax > 0.0f && amax <= 3.402823466e38f) ? __fdiv_rn(amax, 2688.0f) : 1.0f;
@@ -1175,6 +1192,14 @@ int nvfp4b200_get_device_error(int* out) {
   if (qe == NVFP4B200_ERR_CUDA) return qe;
   if (*out == 0) *out = qe;
   return NVFP4B200_OK;
+}
+
+int nvfp4b200_wait_selftest(int64_t limit_cycles, void* stream) {
+  if (limit_cycles < 1 || limit_cycles > (1ll << 32)) return NVFP4B200_ERR_INVALID_ARG;
+  int rc = check_device();
+  if (rc) return rc;
+  gemm::wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>((long long)limit_cycles);
+  return launch_status();
 }
 
 int nvfp4b200_set_gemm_max_sms(int max_sms) {
