@@ -173,6 +173,17 @@ int nvfp4b200_global_scale_noalloc(const void* x, int64_t n, float* global_scale
  * output_scale: device float (NULL = 1); bias: bf16 [n] or NULL;
  * d: bf16 [m, n] row-major.  Constraints: k % 32 == 0, n % 8 == 0, all
  * pointers 16-byte aligned. */
+/* gn_kernels::cutlass_sm120a_mxfp4_mm (cutlass_mm_fp4.cu:71-165): MXFP4
+ *   d = bf16(A . B^T + bias)
+ * with E2M1 operands and one UE8M0 scale (2^(e-127)) per 1x32 block along k.
+ * a: packed [m, k/2]; b: packed [n, k/2]; sfa / sfb: the 128x4-atom swizzled
+ * layout with one column per 32 k, i.e. [round_up(rows, 128),
+ * round_up(k/32, 4)] bytes; padding entries must not be 0xFF (NaN).
+ * bias: bf16 [n] or NULL; d: bf16 [m, n].  k % 32 == 0, n % 8 == 0, all
+ * pointers 16-byte aligned. */
+int nvfp4b200_mxfp4_mm(const void* a, const void* b, const void* sfa, const void* sfb, const void* bias, void* d,
+                       int64_t m, int64_t n, int64_t k, void* stream);
+
 int nvfp4b200_nvfp4_mm(const void* a, const void* b, const void* sfa, const void* sfb,
                        const float* output_scale, const void* bias, void* d,
                        int64_t m, int64_t n, int64_t k, void* stream);

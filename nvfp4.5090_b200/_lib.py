@@ -35,6 +35,7 @@ SIGNATURES = {
     "nvfp4b200_global_scale": [c_void_p, c_i64, c_void_p, c_void_p, c_void_p, c_void_p],
     "nvfp4b200_global_scale_noalloc": [c_void_p, c_i64, c_void_p, c_void_p, c_void_p],
     "nvfp4b200_nvfp4_mm": [c_void_p] * 7 + [c_i64] * 3 + [c_void_p],
+    "nvfp4b200_mxfp4_mm": [c_void_p] * 6 + [c_i64] * 3 + [c_void_p],
     "nvfp4b200_nvfp4_mm_relu": [c_void_p] * 7 + [c_i64] * 3 + [c_void_p],
     "nvfp4b200_nvfp4_mm_relu_2": [c_void_p] * 7 + [c_i64] * 3 + [c_void_p],
     "nvfp4b200_gemm": [c_void_p] * 9 + [c_int] * 3 + [c_i64] * 4 + [c_void_p],

@@ -66,6 +66,12 @@ constexpr int SFB_BYTES = 1024 * KBLOCKS;             // 2 row groups x 4 atoms
 constexpr int SFB_G1 = 512 * KBLOCKS;                 // offset of B's second row group
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
 constexpr uint32_t STAGE_TX = 2u * STAGE_BYTES;       // bytes landing per stage across the pair
+// MXFP4 (1x32 blocks, UE8M0 scales): a stage's 256 k hold 8 scales per row,
+// i.e. 2 atoms per 128-row group; the scale buffers are half used.
+constexpr int SFA_BYTES_MX = 256 * KBLOCKS;
+constexpr int SFB_BYTES_MX = 512 * KBLOCKS;
+constexpr int SFB_G1_MX = 256 * KBLOCKS;
+constexpr uint32_t STAGE_TX_MX = 2u * (A_BYTES + B_BYTES + SFA_BYTES_MX + SFB_BYTES_MX);
 constexpr int EPI_WARPS = 8;
 constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS);
 constexpr int TMEM_COLS = 512;
@@ -96,6 +102,11 @@ constexpr int GROUP_M = 8;                            // raster: 8 pair-rows (20
 constexpr uint32_t IDESC =
     (1u << 7) | (1u << 10) | ((uint32_t)(TILE_N >> 3) << 17) | ((uint32_t)(TILE_M >> 4) << 24);
 
+// kind::mxf4 (MXFP4): same fields, UE8M0 scales (bit 23); the scale-factor IDs
+// (bits 4-5 for B, 29-30 for A) are set per MMA.
+constexpr uint32_t IDESC_MX =
+    (1u << 7) | (1u << 10) | ((uint32_t)(TILE_N >> 3) << 17) | (1u << 23) | ((uint32_t)(TILE_M >> 4) << 24);
+
 struct Params {
   const float* scale_a;
   const float* scale_b;
@@ -103,7 +114,7 @@ struct Params {
   const uint16_t* residual;  // bf16 [m, n], row stride ldd, added after the activation
   void* d;
   int64_t m, n, k, ldd;
-  int64_t sf_atoms;          // scale atoms per 128-row group = ceil(k/64)
+  int64_t sf_atoms;          // scale atoms per 128-row group = ceil(k/64), or ceil(k/128) for MXFP4
   int num_m_tiles, num_n_tiles, num_k_tiles;
   int d_f32, accumulate, epilogue;
   int swiglu;                // B rows interleaved [gate 128 | up 128] per tile: d = silu(gate)*up
@@ -112,6 +123,7 @@ struct Params {
   int dswiglu;               // D = dh -> dgu = SwiGLU backward against gate/up (tmap_h loads, tmap_d stores)
   int stages;                // pipeline stages in use (STAGES, or DSW_STAGES with dswiglu)
   int out_bytes;             // epilogue staging bytes (OUT_BYTES or DSW_OUT_BYTES)
+  int mx;                    // MXFP4 operands: 1x32 blocks, UE8M0 scales (kind::mxf4)
 };
 
 // ---------------------------------------------------------------------------
@@ -304,6 +316,21 @@ __device__ __forceinline__ void tc_mma_pair(uint32_t d, uint64_t adesc, uint64_t
       "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate), "r"(sfa), "r"(sfb)
       : "memory");
 }
+// MXFP4 MMA (kind::mxf4, 1x32 blocks).  A 4-byte TMEM scale cell holds the
+// scales of 128 k, two MMAs' worth: the byte the MMA starts at (0 or 2) is
+// given both in the scale addresses' two top bits and in the descriptor's
+// scale-factor ID fields.
+__device__ __forceinline__ void tc_mma_pair_mx(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t sfa, uint32_t sfb,
+                                               uint32_t sf_byte, uint32_t accumulate) {
+  const uint32_t idesc = IDESC_MX | (sf_byte << 29) | (sf_byte << 4);
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+          d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa | (sf_byte << 30)), "r"(sfb | (sf_byte << 30))
+      : "memory");
+}
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -484,9 +511,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         const uint32_t lbar = map_to_rank(full_bar(stage), 0);
-        const int sf_dy = 2 * KBLOCKS * kt;
+        const int sf_dy = (p.mx ? KBLOCKS : 2 * KBLOCKS) * kt;   // scale rows of 256 bytes per stage
         if (elect_one()) {
-          if (leader) mbar_expect_tx(full_bar(stage), STAGE_TX);
+          if (leader) mbar_expect_tx(full_bar(stage), p.mx ? STAGE_TX_MX : STAGE_TX);
           tma_load_2d_pair(smem_u32(sA + stage * A_BYTES), &tmap_a, lbar, kt * BK_BYTES, a_row);
           tma_load_2d_pair(smem_u32(sB + stage * B_BYTES), &tmap_b, lbar, kt * BK_BYTES, b_row);
           tma_load_2d_pair(smem_u32(sSFA + stage * SFA_BYTES), &tmap_sfa, lbar, 0, (int)(sfa_row0 + sf_dy));
@@ -545,12 +572,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           const uint64_t sfa_d = desc_scales(smem_u32(sSFA + stage * SFA_BYTES));
           const uint64_t sfb_d = desc_scales(smem_u32(sSFB + stage * SFB_BYTES));
           if (elect_one()) {
-            for (int j = 0; j < nkb; ++j) {
-              tc_cp_scales_pair(sfa_t + 4 * j, sfa_d + 32 * j);  // +512 bytes per atom
-              tc_cp_scales_pair(sfb_t + 8 * j, sfb_d + 32 * j);
-              tc_cp_scales_pair(sfb_t + 8 * j + 4, sfb_d + (SFB_G1 >> 4) + 32 * j);
-              // advance 32 bytes (64 fp4) along K inside the swizzled row
-              tc_mma_pair(acc, adesc + 2 * j, bdesc + 2 * j, sfa_t + 4 * j, sfb_t + 8 * j, (kt | j) != 0);
+            if (!p.mx) {
+              for (int j = 0; j < nkb; ++j) {
+                tc_cp_scales_pair(sfa_t + 4 * j, sfa_d + 32 * j);  // +512 bytes per atom
+                tc_cp_scales_pair(sfb_t + 8 * j, sfb_d + 32 * j);
+                tc_cp_scales_pair(sfb_t + 8 * j + 4, sfb_d + (SFB_G1 >> 4) + 32 * j);
+                // advance 32 bytes (64 fp4) along K inside the swizzled row
+                tc_mma_pair(acc, adesc + 2 * j, bdesc + 2 * j, sfa_t + 4 * j, sfb_t + 8 * j, (kt | j) != 0);
+              }
+            } else {
+              for (int j = 0; j < nkb; ++j) {
+                const int a = j >> 1;   // an atom's 4 scales per row cover the 128 k of MMAs 2a, 2a + 1
+                if ((j & 1) == 0) {
+                  tc_cp_scales_pair(sfa_t + 4 * a, sfa_d + 32 * a);
+                  tc_cp_scales_pair(sfb_t + 8 * a, sfb_d + 32 * a);
+                  tc_cp_scales_pair(sfb_t + 8 * a + 4, sfb_d + (SFB_G1_MX >> 4) + 32 * a);
+                }
+                tc_mma_pair_mx(acc, adesc + 2 * j, bdesc + 2 * j, sfa_t + 4 * a, sfb_t + 8 * a, 2u * (j & 1),
+                               (kt | j) != 0);
+              }
             }
             tc_commit_pair(empty_bar(stage));
           }
@@ -991,13 +1031,14 @@ static bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t r
 
 // Scale tensor as [groups][rows_per_group][256 bytes] (a 128-row group's
 // atoms are rows_per_group rows of 256 bytes); one box = one k-slab
-// (2 * KBLOCKS rows) of two consecutive groups.  Groups past the end read zeros.
-static bool make_map_sf_groups(CUtensorMap* map, const void* base, int64_t groups, int64_t rows_per_group) {
+// (box_rows rows) of two consecutive groups.  Groups past the end read zeros.
+static bool make_map_sf_groups(CUtensorMap* map, const void* base, int64_t groups, int64_t rows_per_group,
+                               int box_rows) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[3] = {256, (cuuint64_t)rows_per_group, (cuuint64_t)groups};
   cuuint64_t strides[2] = {256, (cuuint64_t)(rows_per_group * 256)};
-  cuuint32_t box[3] = {256, (cuuint32_t)(2 * KBLOCKS), 2};
+  cuuint32_t box[3] = {256, (cuuint32_t)box_rows, 2};
   cuuint32_t estr[3] = {1, 1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1086,7 +1127,7 @@ struct DswigluIn {
 static int run(const void* a, const void* b, const void* sfa, const void* sfb, const float* scale_a,
                const float* scale_b, const void* bias, const void* residual, void* d, int d_dtype, int accumulate,
                int epilogue, int64_t m, int64_t n, int64_t k, int64_t ldd, cudaStream_t stream,
-               const SwigluOut* sw = nullptr, const DswigluIn* dsw = nullptr) {
+               const SwigluOut* sw = nullptr, const DswigluIn* dsw = nullptr, int mx = 0) {
   if (!a || !b || !sfa || !sfb || !d) return NVFP4B200_ERR_INVALID_ARG;
   if (d_dtype != NVFP4B200_BF16 && d_dtype != NVFP4B200_F32) return NVFP4B200_ERR_INVALID_ARG;
   if (epilogue < 0 || epilogue > 2) return NVFP4B200_ERR_INVALID_ARG;
@@ -1101,7 +1142,10 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   if (rc) return rc;
   if (m == 0 || n == 0) return NVFP4B200_OK;
 
-  const int64_t sf_atoms = ceil_div(k, 64);
+  // scale atoms (512 bytes: 128 rows x 4 scales) per 128-row group: 64 k each
+  // (NVFP4, 1x16 blocks) or 128 k each (MXFP4, 1x32 blocks)
+  const int64_t sf_atoms = ceil_div(k, mx ? 128 : 64);
+  const int sf_box_rows = mx ? KBLOCKS : 2 * KBLOCKS;
   const int64_t pad_m = round_up(m, 128), pad_n = round_up(n, 128);
   CUtensorMap ma, mb, msa, msb, md;
   memset(&md, 0, sizeof(md));
@@ -1109,8 +1153,8 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   const CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B;
   if (!make_map(&ma, a, m, k / 2, BK_BYTES, CTA_M, swz) ||
       !make_map(&mb, b, n, k / 2, BK_BYTES, CTA_N, swz) ||
-      !make_map(&msa, sfa, pad_m * sf_atoms * 4 / 256, 256, 256, 2 * KBLOCKS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map_sf_groups(&msb, sfb, pad_n / 128, sf_atoms * 2))
+      !make_map(&msa, sfa, pad_m * sf_atoms * 4 / 256, 256, 256, sf_box_rows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map_sf_groups(&msb, sfb, pad_n / 128, sf_atoms * 2, sf_box_rows))
     return NVFP4B200_ERR_CUDA;
   // bf16 output viewed as bytes: [m rows, 2n bytes], row stride 2*ldd, boxes of 32 rows x 128 bytes
   CUtensorMap mh;
@@ -1151,6 +1195,7 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   p.store_gu = (sw && sw->gu) ? 1 : 0;
   p.h_amax = sw ? sw->ws : (dsw ? dsw->ws : nullptr);
   p.dswiglu = dsw ? 1 : 0;
+  p.mx = mx;
   p.stages = dsw ? DSW_STAGES : STAGES;
   p.out_bytes = dsw ? DSW_OUT_BYTES : OUT_BYTES;
   const int smem_bytes = dsw ? DSW_SMEM_BYTES : SMEM_BYTES;
@@ -1241,6 +1286,12 @@ int nvfp4b200_nvfp4_mm(const void* a, const void* b, const void* sfa, const void
                        const void* bias, void* d, int64_t m, int64_t n, int64_t k, void* stream) {
   return gemm::run(a, b, sfa, sfb, output_scale, nullptr, bias, nullptr, d, NVFP4B200_BF16, 0, NVFP4B200_EPI_NONE, m,
                    n, k, n, (cudaStream_t)stream);
+}
+
+int nvfp4b200_mxfp4_mm(const void* a, const void* b, const void* sfa, const void* sfb, const void* bias, void* d,
+                       int64_t m, int64_t n, int64_t k, void* stream) {
+  return gemm::run(a, b, sfa, sfb, nullptr, nullptr, bias, nullptr, d, NVFP4B200_BF16, 0, NVFP4B200_EPI_NONE, m, n, k,
+                   n, (cudaStream_t)stream, nullptr, nullptr, /*mx=*/1);
 }
 
 int nvfp4b200_nvfp4_mm_relu(const void* a, const void* b, const void* sfa, const void* sfb, const float* output_scale,

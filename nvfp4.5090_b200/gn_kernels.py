@@ -80,8 +80,28 @@ def _define(name: str):
     return op
 
 
+@torch.library.custom_op("nvfp4_b200::cutlass_mxfp4_mm", mutates_args=(), device_types="cuda")
+def cutlass_mxfp4_mm(A: torch.Tensor, B: torch.Tensor, scales_A: torch.Tensor, scales_B: torch.Tensor,
+                     bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """MXFP4 op of cutlass_mm_fp4.cu:71-165: bf16(A . B^T + bias) with UE8M0
+    scales per 1x32 block (no output scale).  A [M, K/2] packed, B the
+    column-major [K/2, N] operand, scales in the 128x4-atom swizzled layout
+    with one column per 32 k."""
+    from .ops import mxfp4_mm
+    if A.dim() != 2 or B.dim() != 2:
+        raise RuntimeError("MXFP4 GEMM expects 2-D operands")
+    if B.size(0) * 2 != A.size(1) * 2:
+        raise RuntimeError(f"K mismatch: A has K={A.size(1) * 2}, B has K={B.size(0) * 2}")
+    return mxfp4_mm(A.contiguous(), scales_A.contiguous(), _b_rows(B), scales_B.contiguous(), bias)
+
+
+@cutlass_mxfp4_mm.register_fake
+def _(A, B, scales_A, scales_B, bias=None):
+    return A.new_empty((A.size(0), B.size(1)), dtype=torch.bfloat16)
+
+
 cutlass_nvfp4_mm = _define("cutlass_nvfp4_mm")
 cutlass_nvfp4_mm_relu = _define("cutlass_nvfp4_mm_relu")
 cutlass_nvfp4_mm_relu_2 = _define("cutlass_nvfp4_mm_relu_2")
 
-__all__ = ["FP4_DTYPE", "cutlass_nvfp4_mm", "cutlass_nvfp4_mm_relu", "cutlass_nvfp4_mm_relu_2"]
+__all__ = ["FP4_DTYPE", "cutlass_nvfp4_mm", "cutlass_nvfp4_mm_relu", "cutlass_nvfp4_mm_relu_2", "cutlass_mxfp4_mm"]

@@ -178,6 +178,37 @@ def set_gemm_max_sms(max_sms: int) -> None:
     _lib.call("nvfp4b200_set_gemm_max_sms", int(max_sms))
 
 
+def mx_scale_shape(rows: int, k: int):
+    """(padded rows, padded columns) of an MXFP4 scale tensor: one UE8M0 scale per 1x32 block."""
+    return ((rows + 127) // 128) * 128, ((k // 32 + 3) // 4) * 4
+
+
+def mxfp4_mm(qa: torch.Tensor, sa: torch.Tensor, qb: torch.Tensor, sb: torch.Tensor,
+             bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """MXFP4 GEMM: D[m, n] = bf16(A . B^T + bias), E2M1 operands with UE8M0 scales per 1x32 block.
+
+    qa: [m, k/2] packed bytes, qb: [n, k/2] packed bytes; sa / sb: swizzled
+    [round_up(rows,128), round_up(k/32,4)] UE8M0 bytes."""
+    _require(qa.is_cuda and qb.is_cuda, "mxfp4_mm requires CUDA tensors")
+    m, kh = qa.shape
+    n, kh2 = qb.shape
+    _require(kh == kh2, f"K mismatch: A has {2 * kh}, B has {2 * kh2}")
+    k = 2 * kh
+    _require(k % 32 == 0, "K must be divisible by 32 for MXFP4 1x32 scaling.")
+    _require(qa.is_contiguous() and qb.is_contiguous() and sa.is_contiguous() and sb.is_contiguous(),
+             "gemm operands must be contiguous")
+    _require(sa.numel() == math.prod(mx_scale_shape(m, k)) and sb.numel() == math.prod(mx_scale_shape(n, k)),
+             "MXFP4 scale tensors must be the padded swizzled [round_up(rows,128), round_up(k/32,4)] layout")
+    if bias is not None:
+        _check_bf16(bias, "bias")
+        _require(bias.numel() == n, "bias is bf16 [n]")
+        bias = bias.contiguous()
+    out = torch.empty((m, n), device=qa.device, dtype=torch.bfloat16)
+    _lib.call("nvfp4b200_mxfp4_mm", qa.data_ptr(), qb.data_ptr(), sa.data_ptr(), sb.data_ptr(), _ptr(bias),
+              out.data_ptr(), m, n, k, _stream(qa))
+    return out
+
+
 def gemm(qa: torch.Tensor, sa: torch.Tensor, qb: torch.Tensor, sb: torch.Tensor, *,
          scale_a: Optional[torch.Tensor] = None, scale_b: Optional[torch.Tensor] = None,
          bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,

@@ -316,6 +316,41 @@ def gemm_emulation_f64(qa, sa, qb, sb, m: int, n: int, k: int,
     return d
 
 
+def ue8m0_decode(code: np.ndarray) -> np.ndarray:
+    """UE8M0 scale byte -> 2^(code - 127) as float64 (0xFF is NaN).  The MXFP4
+    scale type of cutlass_mm_fp4.cu:79 (``mx_float4_t<float_e2m1_t>``)."""
+    c = np.asarray(code, dtype=np.int64)
+    out = np.ldexp(1.0, c - 127)
+    return np.where(c == 255, np.nan, out)
+
+
+def mx_scale_shape(rows: int, k: int) -> Tuple[int, int]:
+    """(pad_R, pad_cols) of an MXFP4 scale tensor: one scale per 1x32 block."""
+    return round_up(rows, 128), round_up(k // 32, 4)
+
+
+def dequant_mxfp4(q: np.ndarray, s: np.ndarray, rows: int, k: int) -> np.ndarray:
+    """e2m1(nibble) * 2^(e - 127) per 1x32 block, as float64.  Scales sit in
+    the same 128x4-atom swizzle as NVFP4's, one column per 32 k."""
+    vals = e2m1_decode(unpack_nibbles(np.asarray(q).reshape(rows, k // 2))).astype(np.float64)
+    pad_r, pad_c = mx_scale_shape(rows, k)
+    flat = np.ascontiguousarray(s, dtype=np.uint8).reshape(-1)
+    assert flat.size == pad_r * pad_c
+    rr, cc = np.meshgrid(np.arange(rows), np.arange(k // 32), indexing="ij")
+    sc = ue8m0_decode(flat[swizzle_offset(rr, cc, pad_c)])
+    return (vals.reshape(rows, k // 32, 32) * sc[:, :, None]).reshape(rows, k)
+
+
+def mxfp4_gemm_emulation_f64(qa, sa, qb, sb, m: int, n: int, k: int,
+                             bias_bf16_bits: Optional[np.ndarray] = None) -> np.ndarray:
+    """float64 value of ``dequant(A) @ dequant(B)^T + bias`` for the MXFP4 op
+    (cutlass_mm_fp4.cu:82-83: bias add then cast, no output scale)."""
+    d = dequant_mxfp4(qa, sa, m, k) @ dequant_mxfp4(qb, sb, n, k).T
+    if bias_bf16_bits is not None:
+        d = d + bf16_bits_to_f32(bias_bf16_bits).astype(np.float64)[None, :]
+    return d
+
+
 def gemm_emulation_bf16(*args, **kw) -> np.ndarray:
     """GEMM emulation rounded to bf16 (returned as float32 values)."""
     d = gemm_emulation_f64(*args, **kw).astype(np.float32)

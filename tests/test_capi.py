@@ -76,7 +76,9 @@ MIS = FAKE + 4
                                         None), 3),                                        # misaligned gate/up
     (lambda L: L.nvfp4b200_gemm_dswiglu(FAKE, FAKE, FAKE, FAKE, None, None, FAKE, FAKE, None, FAKE, 8, 512, 64,
                                         None), 1),                                        # g_out without ws
-    (lambda L: L.nvfp4b200_wait_selftest(0, None), 1),                                  # limit out of range
+    (lambda L: L.nvfp4b200_wait_selftest(0, None), 1),
+    (lambda L: L.nvfp4b200_mxfp4_mm(FAKE, FAKE, FAKE, FAKE, None, FAKE, 8, 8, 48, None), 2),        # k % 32
+    (lambda L: L.nvfp4b200_mxfp4_mm(None, FAKE, FAKE, FAKE, None, FAKE, 8, 8, 64, None), 1),                                  # limit out of range
     (lambda L: L.nvfp4b200_adamw_step(FAKE, FAKE, 5, FAKE, FAKE, 8, 1e-3, .9, .95, 1e-8, 0., 1., 1., 1., None), 1),
 ])
 def test_argument_validation_without_device(pkg, call, expected):

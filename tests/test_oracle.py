@@ -204,3 +204,21 @@ def test_gemm_emulation_matches_reference_gemm_golden():
         assert err < 1e-2, (name, err)
         # bf16 output rounding bounds the element error (plus accumulation slack)
         assert np.all(np.abs(ref - emu) <= np.abs(emu) * 2.0 ** -8 + 1e-3 * math.sqrt(k)), name
+
+
+def test_mxfp4_dequant_known_answer():
+    """UE8M0 scales are powers of two (2^(e-127), 0xFF NaN) applied per 1x32
+    block through the 128x4-atom swizzle; nibbles decode as E2M1."""
+    assert orc.ue8m0_decode(np.array([127, 128, 120, 0]))[:3].tolist() == [1.0, 2.0, 2.0 ** -7]
+    assert np.isnan(orc.ue8m0_decode(np.array([255])))[0]
+    rows, k = 3, 64
+    q = np.zeros((rows, k // 2), dtype=np.uint8)
+    q[1, 0] = 0x2F       # row 1: element 0 = -6 (0xF), element 1 = +1 (0x2)
+    q[2, 16] = 0x07      # row 2: element 32 = +6 (second block)
+    pad_r, pad_c = orc.mx_scale_shape(rows, k)
+    s = np.zeros(pad_r * pad_c, dtype=np.uint8)
+    s[orc.swizzle_offset(np.array(1), np.array(0), pad_c)] = 129   # x4
+    s[orc.swizzle_offset(np.array(2), np.array(1), pad_c)] = 126   # x1/2
+    d = orc.dequant_mxfp4(q, s, rows, k)
+    assert d[1, 0] == -24.0 and d[1, 1] == 4.0 and d[2, 32] == 3.0
+    assert np.count_nonzero(d) == 3
