@@ -264,6 +264,39 @@ def bench_gemm(pkg, args, world, rank, peaks):
         except Exception as e:  # keep the bench line even if the library path is unavailable
             res["cublaslt_scaled_mm_tflops"] = None
             res["cublaslt_error"] = f"{type(e).__name__}: {str(e)[:160]}"
+    # MXFP4 GEMM (cutlass_mm_fp4.cu:71-165: UE8M0 scales per 1x32 block), same shape, outside the headline
+    if rank == 0:
+        gm = torch.Generator(device="cuda").manual_seed(6)
+        mqa = torch.randint(0, 256, (m, k // 2), dtype=torch.uint8, device="cuda", generator=gm)
+        mqb = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device="cuda", generator=gm)
+        msa = torch.randint(120, 135, pkg.ops.mx_scale_shape(m, k), dtype=torch.uint8, device="cuda", generator=gm)
+        msb = torch.randint(120, 135, pkg.ops.mx_scale_shape(n, k), dtype=torch.uint8, device="cuda", generator=gm)
+        mrun = lambda: pkg.ops.mxfp4_mm(mqa, msa, mqb, msb)
+        for _ in range(3):
+            mrun()
+        mt = timed_launches(mrun, args.steps, flush)
+        mtf = flops / (sum(mt) / len(mt) * 1e-3) / 1e12
+        mx = {"tflops": mtf, "frac": mtf / fp4_peak, "unit": "TFLOP/s",
+              "workload": "MXFP4 GEMM M=N=K=8192 (random E2M1, UE8M0 scales 2^-7..2^7, seed 6), L2 flushed"}
+        if not args.no_cublas:
+            try:
+                import torch.nn.functional as F
+                from torch.nn.functional import ScalingType, SwizzleType
+                ma4, mb4 = mqa.view(torch.float4_e2m1fn_x2), mqb.view(torch.float4_e2m1fn_x2)
+                ms_a, ms_b = msa.view(torch.float8_e8m0fnu), msb.view(torch.float8_e8m0fnu)
+                mcub = lambda: F.scaled_mm(ma4, mb4.mT, ms_a, ScalingType.BlockWise1x32, ms_b,
+                                           ScalingType.BlockWise1x32, swizzle_a=SwizzleType.SWIZZLE_32_4_4,
+                                           swizzle_b=SwizzleType.SWIZZLE_32_4_4, output_dtype=torch.bfloat16,
+                                           contraction_dim=(1, 0))
+                for _ in range(3):
+                    mcub()
+                mct = timed_launches(mcub, args.steps, flush)
+                mx["cublaslt_scaled_mm_tflops"] = flops / (sum(mct) / len(mct) * 1e-3) / 1e12
+            except Exception as e:
+                mx["cublaslt_scaled_mm_tflops"] = None
+                mx["cublaslt_error"] = f"{type(e).__name__}: {str(e)[:160]}"
+        res["mxfp4"] = mx
+        del mqa, mqb, msa, msb
     # e2e through the reference-shaped C-ABI op with host buffers (pinned), H2D + D2H in the timed region
     hqa = qa.cpu().pin_memory()
     hqb = qb.cpu().pin_memory()
@@ -632,6 +665,8 @@ def main(argv=None):
             "spot_check_max_rel_err": gemm["spot_check_max_rel_err"]}
     if "m_sweep" in gemm:
         line["gemm_m_sweep"] = gemm["m_sweep"]
+    if "mxfp4" in gemm:
+        line["mxfp4_gemm_8192"] = gemm["mxfp4"]
     if "cublaslt_error" in gemm:
         line["cublaslt_error"] = gemm["cublaslt_error"]
     if rank == 0 and world == 1 and "cpu" not in skip:
