@@ -90,3 +90,22 @@ def test_python_binding_fails_loudly_without_library(pkg, monkeypatch, tmp_path)
     monkeypatch.setattr(pkg._lib, "lib_path", lambda: str(tmp_path / "missing.so"))
     with pytest.raises(pkg.NVFP4Error):
         pkg._lib.load()
+
+
+def test_gn_kernels_ops_trace_with_fake_tensors(pkg):
+    """The torch custom ops (NVFP4 and MXFP4 GEMMs) have fake implementations:
+    under FakeTensorMode they give the bf16 [M, N] result without a device,
+    which is what torch.compile tracing needs."""
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    from nvfp4_b200 import gn_kernels as g
+    with FakeTensorMode():
+        a = torch.empty(300, 256, dtype=torch.uint8, device="cuda")
+        b = torch.empty(264, 256, dtype=torch.uint8, device="cuda")
+        s = torch.empty(384, 16, dtype=torch.uint8, device="cuda")
+        one = torch.empty((), dtype=torch.float32, device="cuda")
+        outs = [g.cutlass_mxfp4_mm(a, b.mT, s, s)] + [op(a, b.mT, s, s, one) for op in
+                                                      (g.cutlass_nvfp4_mm, g.cutlass_nvfp4_mm_relu,
+                                                       g.cutlass_nvfp4_mm_relu_2)]
+    for d in outs:
+        assert tuple(d.shape) == (300, 264) and d.dtype == torch.bfloat16
