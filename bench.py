@@ -302,34 +302,37 @@ def bench_gemm(pkg, args, world, rank, peaks):
     hqb = qb.cpu().pin_memory()
     hsa = sa.cpu().pin_memory()
     hsb = sb.cpu().pin_memory()
-    hout = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
-    dqa, dqb, dsa, dsb = torch.empty_like(qa), torch.empty_like(qb), torch.empty_like(sa), torch.empty_like(sb)
+    # two device slots: step i + 1's inputs upload while step i computes and step i - 1's result downloads
+    hout = [torch.empty((m, n), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    dev = [(torch.empty_like(qa), torch.empty_like(qb), torch.empty_like(sa), torch.empty_like(sb),
+            torch.empty((m, n), device="cuda", dtype=torch.bfloat16)) for _ in range(2)]
     scale = (ga * gb).reshape(())
 
-    def e2e_step():
+    def upload(i, b):
+        dqa, dqb, dsa, dsb, _ = dev[b]
         dqa.copy_(hqa, non_blocking=True)
         dqb.copy_(hqb, non_blocking=True)
         dsa.copy_(hsa, non_blocking=True)
         dsb.copy_(hsb, non_blocking=True)
-        pkg.ops._lib.call("nvfp4b200_nvfp4_mm", dqa.data_ptr(), dqb.data_ptr(), dsa.data_ptr(), dsb.data_ptr(),
-                          scale.data_ptr(), None, out.data_ptr(), m, n, k,
-                          torch.cuda.current_stream().cuda_stream)
-        hout.copy_(out, non_blocking=True)
 
-    e2e_step()
+    def compute(i, b):
+        dqa, dqb, dsa, dsb, dout = dev[b]
+        pkg.ops._lib.call("nvfp4b200_nvfp4_mm", dqa.data_ptr(), dqb.data_ptr(), dsa.data_ptr(), dsb.data_ptr(),
+                          scale.data_ptr(), None, dout.data_ptr(), m, n, k,
+                          torch.cuda.current_stream().cuda_stream)
+
+    def download(i, b):
+        hout[b].copy_(dev[b][4], non_blocking=True)
+
+    pipelined_e2e(2, upload, compute, download)   # warm-up
     barrier(world)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_ms = max_over_ranks(pipelined_e2e(args.steps, upload, compute, download), world)
+    out = dev[(args.steps - 1) % 2][4]
     h2d = qa.numel() + qb.numel() + sa.numel() + sb.numel()
     res["e2e"] = {"value": world * flops * args.steps / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out.numel() * 2,
-                  "path": "nvfp4b200_nvfp4_mm C ABI (gn_kernels::cutlass_sm120a_nvfp4_mm contract)"}
+                  "path": "nvfp4b200_nvfp4_mm C ABI (gn_kernels::cutlass_sm120a_nvfp4_mm contract)",
+                  "pipeline": PIPELINE_NOTE}
     # correctness spot check against float64 (a few elements)
     res["spot_check_max_rel_err"] = gemm_spot_check(qa, sa, qb, sb, out, ga, gb)
     # M sweep at N = K = 8192 (same B operand), ours and cuBLASLt, L2 flushed per launch
@@ -443,7 +446,8 @@ def bench_quant(pkg, args, peaks):
 # MLP training steps
 # ---------------------------------------------------------------------------
 
-def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=None, micro_tokens=16384):
+def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=None, micro_tokens=16384,
+              e2e_steps=None):
     import torch
     from nvfp4_b200.mlp import NVFP4MLPStackTrainer
     t_local = global_tokens // world
@@ -474,26 +478,85 @@ def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=No
     # e2e through the public API: pinned host tokens + upstream grad copied in, step result read back
     hx = x.cpu().pin_memory()
     hdy = dy.cpu().pin_memory()
-    hres = torch.empty(1, dtype=torch.float32).pin_memory()
-    dx, ddy = torch.empty_like(x), torch.empty_like(dy)
+    hres = [torch.empty(1, dtype=torch.float32).pin_memory() for _ in range(2)]
+    slots = [(torch.empty_like(x), torch.empty_like(dy)) for _ in range(2)]
+    results = []   # step results stay referenced until the run ends (read on the download stream)
+
+    def upload(i, b):
+        slots[b][0].copy_(hx, non_blocking=True)
+        slots[b][1].copy_(hdy, non_blocking=True)
+
+    def compute(i, b):
+        results.append(trainer.step(slots[b][0], slots[b][1]))
+
+    def download(i, b):
+        hres[b].copy_(results[i], non_blocking=True)
+
+    n_e2e = max(2, e2e_steps if e2e_steps is not None else args.steps // 2)
     barrier(world)
-    e0.record()
-    for _ in range(max(1, args.steps // 2)):
-        dx.copy_(hx, non_blocking=True)
-        ddy.copy_(hdy, non_blocking=True)
-        r = trainer.step(dx, ddy)
-        hres.copy_(r, non_blocking=True)
-    trainer.finish()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / max(1, args.steps // 2)
+    e2e_ms = max_over_ranks(pipelined_e2e(n_e2e, upload, compute, download, finish=trainer.finish), world) / n_e2e
+    del results[:]
     res["e2e"] = {"value": global_tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
-                  "h2d_bytes_per_step": 2 * x.numel() * 2 * world, "d2h_bytes_per_step": 4 * world}
+                  "h2d_bytes_per_step": 2 * x.numel() * 2 * world, "d2h_bytes_per_step": 4 * world,
+                  "pipeline": PIPELINE_NOTE}
     if getattr(args, "breakdown", False) and world == 1:
         res["kernel_breakdown"] = step_breakdown(trainer, x, dy, n_blocks, d, f, micro_tokens)
     del trainer
     torch.cuda.empty_cache()
     return res
+
+
+PIPELINE_NOTE = ("every step uploads its inputs from pinned host memory and downloads its result inside the "
+                 "timed region; step i + 1's upload and step i's download overlap step i's compute (two device "
+                 "slots, one copy stream per direction, ordered by events)")
+
+
+def pipelined_e2e(steps, upload, compute, download, finish=None):
+    """Time `steps` end-to-end steps: upload(i, slot) copies step i's inputs
+    host -> device on an upload stream, compute(i, slot) runs the step on the
+    current stream, download(i, slot) copies its result device -> host on a
+    download stream.  Two slots: step i + 1's upload overlaps step i's compute,
+    and step i's download overlaps step i + 1.  Returns the device time (ms)
+    from before the first upload to after the last download."""
+    import torch
+    comp = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_comp = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    s_in.wait_event(e0)
+
+    def up(i):
+        b = i % 2
+        if i >= 2:
+            s_in.wait_event(ev_comp[b])      # step i - 2 has finished with slot b
+        with torch.cuda.stream(s_in):
+            upload(i, b)
+        ev_in[b].record(s_in)
+
+    up(0)
+    for i in range(steps):
+        b = i % 2
+        if i + 1 < steps:
+            up(i + 1)
+        comp.wait_event(ev_in[b])
+        if i >= 2:
+            comp.wait_event(ev_out[b])       # step i - 2's result has been read out of slot b
+        compute(i, b)
+        ev_comp[b].record(comp)
+        s_out.wait_event(ev_comp[b])
+        with torch.cuda.stream(s_out):
+            download(i, b)
+        ev_out[b].record(s_out)
+    if finish is not None:
+        finish()
+    comp.wait_stream(s_out)
+    comp.wait_stream(s_in)
+    e1.record(comp)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
 
 
 def step_breakdown(trainer, x, dy, n_blocks, d, f, micro):
@@ -640,7 +703,7 @@ def main(argv=None):
         elif args.only == "quant":
             res = bench_quant(pkg, args, peaks)
         elif args.only == "mlp_block":
-            res = bench_mlp(pkg, args, world, rank, 1, 4096, 14336, 16384, seed=3)
+            res = bench_mlp(pkg, args, world, rank, 1, 4096, 14336, 16384, seed=3, e2e_steps=args.steps)
         else:
             res = bench_mlp(pkg, args, world, rank, 8, 8192, 28672, 65536, seed=4, pg=pg)
         if rank == 0:
@@ -677,7 +740,7 @@ def main(argv=None):
     if world == 1 and "quant" not in skip:
         line["quant"] = bench_quant(pkg, args, peaks)
     if world == 1 and "mlp_block" not in skip:
-        line["mlp_block"] = bench_mlp(pkg, args, world, rank, 1, 4096, 14336, 16384, seed=3)
+        line["mlp_block"] = bench_mlp(pkg, args, world, rank, 1, 4096, 14336, 16384, seed=3, e2e_steps=args.steps)
         line["mlp_block"]["workload"] = "1 RMSNorm+SwiGLU block, 16384 tokens, d=4096, ff=14336, AdamW fp32"
     if "mlp_stack" not in skip:
         line["mlp_stack"] = bench_mlp(pkg, args, world, rank, 8, 8192, 28672, 65536, seed=4, pg=pg)
