@@ -36,6 +36,13 @@
 // The producer, MMA and epilogue loops run on converged warps; TMA, copy and
 // MMA instructions are issued by one elect.sync-chosen lane from warp-uniform
 // operands.
+// Modes (launch parameters of the same kernel):
+//   NVFP4 (kind::mxf4nvf4, E4M3 scale per 1x16 block) or MXFP4 (kind::mxf4,
+//   UE8M0 scale per 1x32 block, cutlass_mm_fp4.cu:71-165);
+//   epilogues: bf16 store (+bias, ReLU / ReLU^2, residual), f32 store or
+//   reduce-add, SwiGLU (gate/up tile -> h, gate/up, max |h|) and SwiGLU
+//   backward (dh tile + TMA-loaded gate/up -> dgu, max |dgu|; 4 stages, the
+//   fifth stage's shared memory holds the gate/up slots).
 // Every mbarrier wait is bounded: on timeout the CTA records
 // NVFP4B200_ERR_TIMEOUT in a device error word, drains what it issued and
 // returns, so a broken pipeline cannot hang the GPU.  No TMA load uses
