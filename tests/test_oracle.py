@@ -222,3 +222,37 @@ def test_mxfp4_dequant_known_answer():
     d = orc.dequant_mxfp4(q, s, rows, k)
     assert d[1, 0] == -24.0 and d[1, 1] == 4.0 and d[2, 32] == 3.0
     assert np.count_nonzero(d) == 3
+
+
+def test_mxfp4_gemm_emulation_matches_scalar_loops():
+    """The MXFP4 emulation (dequantize, float64 matmul) against plain scalar
+    loops that decode every nibble and scale on their own: E2M1 magnitudes
+    {0, .5, 1, 1.5, 2, 3, 4, 6} with the sign in bit 3, element 2j in the low
+    nibble, scale of (row r, block c) at the 128x4-atom position, 2^(e-127)."""
+    rng = np.random.default_rng(3)
+    m, n, k = 5, 3, 96                     # three 32-element blocks: a partial 4-block group
+    mags = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
+
+    def operand(rows):
+        q = rng.integers(0, 256, size=(rows, k // 2), dtype=np.uint8)
+        pad_r, pad_c = orc.round_up(rows, 128), orc.round_up(k // 32, 4)
+        s = np.zeros(pad_r * pad_c, dtype=np.uint8)
+        codes = rng.integers(120, 135, size=(rows, k // 32))
+        for r in range(rows):
+            for c in range(k // 32):
+                pos = ((r // 128) * (pad_c // 4) + c // 4) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + c % 4
+                s[pos] = codes[r, c]
+        return q, s, codes
+
+    def value(q, codes, r, j):
+        byte = int(q[r, j // 2])
+        nib = byte & 0xF if j % 2 == 0 else byte >> 4
+        v = mags[nib & 7] * (-1.0 if nib & 8 else 1.0)
+        return v * 2.0 ** (int(codes[r, j // 32]) - 127)
+
+    qa, sa, ca = operand(m)
+    qb, sb, cb = operand(n)
+    ref = np.array([[sum(value(qa, ca, i, j) * value(qb, cb, t, j) for j in range(k)) for t in range(n)]
+                    for i in range(m)])
+    got = orc.mxfp4_gemm_emulation_f64(qa, sa, qb, sb, m, n, k)
+    assert np.array_equal(got, ref) or np.allclose(got, ref, rtol=1e-12, atol=0)
