@@ -451,7 +451,7 @@ __device__ __forceinline__ bool tq_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 template <bool HAS_ROW, bool HAS_GAMMA>
-__global__ void __launch_bounds__(256) quant_t_kernel(
+__global__ void __launch_bounds__(256, 3) quant_t_kernel(
     const __grid_constant__ CUtensorMap xmap, const float* __restrict__ row_scale,
     const uint16_t* __restrict__ gamma, uint8_t* __restrict__ q, uint8_t* __restrict__ s, int64_t rows,
     int64_t cols, int64_t pad_cols_out, int n_tiles_t, int n_tiles, const float* __restrict__ gptr, int q16) {
