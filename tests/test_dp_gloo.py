@@ -1,4 +1,4 @@
-"""Data-parallel host logic on CPU with world_size-2 gloo process groups:
+"""Data-parallel host logic on CPU with gloo process groups of 2 and 4 ranks:
 bucketed async all-reduce, mean-gradient scaling, the ZeRO-1 sharded
 optimizer (reduce-scatter, shard update, all-gather) against the all-reduce
 path, and host-side failure detection (a rank that dies before the
@@ -167,14 +167,16 @@ def _run(target, world=2, timeout=60):
     return out
 
 
-def test_bucketed_allreduce_two_ranks():
-    out = _run(_worker_reduce)
-    assert out == {0: "ok", 1: "ok"}, out
+@pytest.mark.parametrize("world", [2, 4])
+def test_bucketed_allreduce(world):
+    out = _run(_worker_reduce, world=world)
+    assert out == {r: "ok" for r in range(world)}, out
 
 
-def test_sharded_optimizer_matches_allreduce_two_ranks():
-    out = _run(_worker_sharded)
-    assert out == {0: "ok", 1: "ok"}, out
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_optimizer_matches_allreduce(world):
+    out = _run(_worker_sharded, world=world)
+    assert out == {r: "ok" for r in range(world)}, out
 
 
 def test_shard_len_pads_evenly():
