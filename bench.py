@@ -672,7 +672,7 @@ def main(argv=None):
     ap.add_argument("--no-clock-hold", action="store_true", help="skip the 1 s sustained clock window (profiling)")
     ap.add_argument("--breakdown", action="store_true",
                     help="after the timed MLP steps, one more step under torch.profiler: per-kernel device time")
-    ap.add_argument("--only", choices=["gemm", "quant", "mlp_block", "mlp_stack"], default=None,
+    ap.add_argument("--only", choices=["gemm", "gemm_sweep", "quant", "mlp_block", "mlp_stack"], default=None,
                     help="run one section and print its result (profiling runs)")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
@@ -700,6 +700,9 @@ def main(argv=None):
     if args.only is not None:
         if args.only == "gemm":
             res = bench_gemm(pkg, args, world, rank, peaks)
+        elif args.only == "gemm_sweep":   # the M sweep alone (N = K = 8192), e.g. to profile one size
+            _, _, qb, sb, _, gb = gemm_operands(pkg, 8, 8192, 8192, seed=1)
+            res = gemm_m_sweep(pkg, args, qb, sb, gb, Flusher(), with_cublas=not args.no_cublas)
         elif args.only == "quant":
             res = bench_quant(pkg, args, peaks)
         elif args.only == "mlp_block":
