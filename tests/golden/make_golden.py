@@ -13,7 +13,7 @@
 
 Usage (on a machine with a B200):
     python oracle/build_ref.py            # in a tree that has the reference
-    python tests/golden/make_golden.py --out gpurun_out/golden
+    python tests/golden/make_golden.py --out /tmp/golden
 and copy the resulting ``golden_*.npz`` next to this file.
 """
 from __future__ import annotations
