@@ -31,6 +31,12 @@ def test_library_exports_every_declared_symbol(pkg):
     assert set(_declared()) == set(pkg._lib.exported_symbols())
 
 
+def test_integration_guide_names_every_entry_point():
+    guide = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    missing = [name for name in _declared() if name not in guide]
+    assert not missing, f"declared in include/nvfp4_b200.h but not described in INTEGRATION.md: {missing}"
+
+
 def test_api_version_matches_header(pkg):
     lib = pkg._lib.load()
     m = re.search(r"#define NVFP4B200_API_VERSION (\d+)", open(HEADER).read())
