@@ -1,0 +1,46 @@
+"""CPU tests of bench.py's host logic: the clock record that decides whether a
+run is kept (median SM clock and the throttle reasons seen), and the reference
+arm's rank handling under torchrun (ranks other than 0 exit without work)."""
+import bench
+
+
+def _sampler(lines):
+    s = bench.ClockSampler(0)
+    s.lines = lines
+    return s.summary()
+
+
+def test_clock_summary_median_and_power_cap():
+    lines = [
+        "0, 1470, 1965, 998.1, 0x4, Not Active, Not Active, Not Active, Active",
+        "0, 1455, 1965, 1001.0, 0x4, Not Active, Not Active, Not Active, Active",
+        "0, 1965, 1965, 420.0, 0x0, Not Active, Not Active, Not Active, Not Active",
+    ]
+    s = _sampler(lines)
+    assert s["sm_mhz"] == 1470 and s["sm_max_mhz"] == 1965 and s["samples"] == 3
+    assert s["reasons"] == ["sw_power_cap"]
+
+
+def test_clock_summary_reports_rejecting_reasons():
+    lines = [
+        "0, 1200, 1965, 700.0, 0x48, Active, Not Active, Not Active, Not Active",
+        "0, 1100, 1965, 690.0, 0x20, Not Active, Not Active, Active, Not Active",
+        "0, 1000, 1965, 650.0, 0x40, Not Active, Active, Not Active, Not Active",
+    ]
+    s = _sampler(lines)
+    assert s["reasons"] == ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown"]
+
+
+def test_clock_summary_skips_malformed_lines():
+    s = _sampler(["garbage", "0, [N/A], 1965, 1.0, 0x0, Not Active, Not Active, Not Active, Not Active",
+                  "0, 1500, 1965, 900.0, 0x0, Not Active, Not Active, Not Active, Not Active"])
+    assert s["sm_mhz"] == 1500 and s["samples"] == 1 and s["reasons"] == []
+    assert _sampler([]) == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+
+
+def test_reference_arm_other_ranks_exit_without_work(monkeypatch, capsys):
+    monkeypatch.setenv("WORLD_SIZE", "2")
+    monkeypatch.setenv("RANK", "1")
+    monkeypatch.setattr(bench, "cpu_gemm_sample", lambda: (_ for _ in ()).throw(AssertionError("ran work")))
+    assert bench.main(["--impl", "reference", "--steps", "1", "--warmup", "3"]) == 0
+    assert capsys.readouterr().out == ""
