@@ -19,7 +19,8 @@ Also reported in the same line:
 
 ``--impl reference`` times the reference path's CPU emulation (quantize,
 dequantize, fp32 matmul: the oracle restatement of float4utils.py) on the
-host cores for the same GEMM metric.  All inputs are seeded synthetic data.
+host cores for the same GEMM metric, one output tile per step.  All inputs
+are seeded synthetic data.
 """
 from __future__ import annotations
 
@@ -611,46 +612,170 @@ def step_breakdown(trainer, x, dy, n_blocks, d, f, micro):
 # reference arm: CPU emulation on the host cores
 # ---------------------------------------------------------------------------
 
-def cpu_gemm_sample(rows: int = 256, n: int = 8192, k: int = 8192, threads=None):
-    """Reference-path CPU emulation (quantize -> dequantize -> fp32 matmul) of a
-    `rows`-row slice of the 8192^3 GEMM.  Returns (TFLOP/s of the matmul
-    part incl. dequantize, cores)."""
+CPU_GEMM_ROWS, CPU_GEMM_COLS = 256, 2048
+
+
+def _cpu_pool(threads=None):
+    """Thread pool over all host cores for the oracle's numpy passes (its
+    large ufuncs release the GIL) and torch's CPU matmuls."""
+    import concurrent.futures
+    import torch
+    cores = threads or os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    return cores, concurrent.futures.ThreadPoolExecutor(cores)
+
+
+def _qdq_rows(x_f32, g, pool, chunk=512):
+    """Oracle quantize (along the last dim, global scale g) then dequantize,
+    in row chunks on the pool; float32 result (exact dequantised values * g)."""
+    import numpy as np
+    from oracle import nvfp4_oracle as orc
+    x_f32 = np.ascontiguousarray(x_f32, dtype=np.float32)
+    r, k = x_f32.shape
+
+    def one(lo):
+        c = x_f32[lo:lo + chunk]
+        q, s = orc.quant_nvfp4_f32(c, g)
+        out = orc.dequant_nvfp4(q, s, c.shape[0], k)
+        return out if g is None else out * np.float32(g)
+
+    return np.concatenate(list(pool.map(one, range(0, r, chunk))), axis=0)
+
+
+def cpu_gemm_sample(rows: int = CPU_GEMM_ROWS, cols: int = CPU_GEMM_COLS, k: int = 8192, threads=None):
+    """Reference-path CPU emulation of a [rows x cols] output tile of the
+    8192^3 GEMM (quantize both operands with per-tensor global scales,
+    dequantize, fp32 torch matmul, bf16 result), all inside the timed region.
+    Returns (TFLOP/s of the tile's 2*rows*cols*k flop, cores, seconds, tile)."""
     import numpy as np
     import torch
     from oracle import nvfp4_oracle as orc
-    cores = threads or os.cpu_count() or 1
-    torch.set_num_threads(cores)
+    cores, pool = _cpu_pool(threads)
     g = torch.Generator().manual_seed(1)
-    a = torch.randn(rows, k, generator=g).to(torch.bfloat16)
-    b = torch.randn(n, k, generator=g).to(torch.bfloat16)
-    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
-    qa, sa = orc.quant_nvfp4(bits(a))
-    qb, sb = orc.quant_nvfp4(bits(b))   # B quantized once (static operand)
+    a = torch.randn(rows, k, generator=g).to(torch.bfloat16).float().numpy()
+    b = torch.randn(cols, k, generator=g).to(torch.bfloat16).float().numpy()
     t0 = time.perf_counter()
-    da = torch.from_numpy(orc.dequant_nvfp4(qa, sa, rows, k))
-    db = torch.from_numpy(orc.dequant_nvfp4(qb, sb, n, k))
-    d = (da @ db.T).to(torch.bfloat16)
+    da = _qdq_rows(a, orc.global_scale_of(a), pool)
+    db = _qdq_rows(b, orc.global_scale_of(b), pool)
+    d = (torch.from_numpy(da) @ torch.from_numpy(db).T).to(torch.bfloat16)
     dt = time.perf_counter() - t0
-    flops = 2.0 * rows * n * k
-    return flops / dt / 1e12, cores, dt, d
+    pool.shutdown()
+    return 2.0 * rows * cols * k / dt / 1e12, cores, dt, d
+
+
+def cpu_quant_sample(rows: int = 2048, k: int = 4096, threads=None):
+    """Reference-path CPU RMSNorm -> NVFP4 (the oracle restatement of
+    float4utils.py:169-295 with gamma and a global scale: 1/RMS, amax of the
+    normalised rows, quantize) on `rows` rows of the 32768 x 4096 workload.
+    Returns (GB/s of algorithmic bytes, cores, seconds)."""
+    import numpy as np
+    import torch
+    from oracle import nvfp4_oracle as orc
+    cores, pool = _cpu_pool(threads)
+    g = torch.Generator().manual_seed(2)
+    rs = torch.exp(torch.empty(rows, 1).uniform_(math.log(0.1), math.log(10.0), generator=g))
+    x = (torch.randn(rows, k, generator=g) * rs).to(torch.bfloat16).float().numpy()
+    gamma = (1 + 0.1 * torch.randn(k, generator=g)).to(torch.bfloat16).float().numpy()
+    t0 = time.perf_counter()
+
+    def stats(lo):
+        c = x[lo:lo + 512].astype(np.float64)
+        inv = (1.0 / np.sqrt(np.mean(c * c, axis=1) + 1e-6)).astype(np.float32)
+        y = (x[lo:lo + 512] * inv[:, None]).astype(np.float32) * gamma[None, :]
+        return inv, y.astype(np.float32)
+
+    parts = list(pool.map(stats, range(0, rows, 512)))
+    y = np.concatenate([p[1] for p in parts])
+    gs = orc.global_scale_of(y)
+    list(pool.map(lambda lo: orc.quant_nvfp4_f32(y[lo:lo + 512], gs), range(0, rows, 512)))
+    dt = time.perf_counter() - t0
+    pool.shutdown()
+    nbytes = orc.bytes_nvfp4_quant(rows, k) + k * 2 + rows * 4
+    return nbytes / dt / 1e9, cores, dt
+
+
+def cpu_mlp_sample(tokens: int = 128, d: int = 4096, f: int = 14336, threads=None):
+    """Reference-path CPU emulation of one NVFP4 SwiGLU MLP block training step
+    (the single-block workload at a reduced token count): every GEMM operand
+    quantized with its global scale along its contraction dimension and
+    dequantized (oracle), fp32 torch matmuls, bf16 rounding where the CUDA
+    step stores bf16, RMSNorm backward, and fp32 AdamW with master weights on
+    all 3*d*f + d parameters.  Returns (tokens/s, cores, seconds)."""
+    import numpy as np
+    import torch
+    from oracle import nvfp4_oracle as orc
+    cores, pool = _cpu_pool(threads)
+    g = torch.Generator().manual_seed(3)
+    bf = lambda t: t.to(torch.bfloat16).float()
+    x = bf(torch.randn(tokens, d, generator=g))
+    w_gu = bf(0.02 * torch.randn(2 * f, d, generator=g))
+    w_down = bf(0.02 * torch.randn(d, f, generator=g))
+    dy = bf(1e-3 * torch.randn(tokens, d, generator=g))
+    params = [w_gu, w_down]
+    master = [p.clone() for p in params]
+    mom = [(torch.zeros_like(p), torch.zeros_like(p)) for p in params]
+    gsc = lambda t: orc.global_scale_of(t.numpy())
+    qdq = lambda t, gg: torch.from_numpy(_qdq_rows(t.contiguous().numpy(), gg, pool))
+    t0 = time.perf_counter()
+    g_gu, g_d = gsc(w_gu), gsc(w_down)
+    wgu_q, wd_q = qdq(w_gu, g_gu), qdq(w_down, g_d)
+    wgu_tq, wd_tq = qdq(w_gu.T, g_gu), qdq(w_down.T, g_d)
+    inv = torch.rsqrt((x.double() ** 2).mean(1) + 1e-6).float()
+    xn = x * inv[:, None]
+    g_xn = gsc(xn)
+    gu = bf(qdq(xn, g_xn) @ wgu_q.T)
+    gate, up = gu[:, :f], gu[:, f:]
+    sg = torch.sigmoid(gate)
+    h = bf(gate * sg * up)
+    g_h = gsc(h)
+    y = bf(qdq(h, g_h) @ wd_q.T + x)
+    g_dy = gsc(dy)
+    dh = bf(qdq(dy, g_dy) @ wd_tq.T)
+    dgu = torch.cat([bf(dh * up * (sg * (1 + gate * (1 - sg)))), bf(dh * gate * sg)], dim=1)
+    g_dgu = gsc(dgu)
+    dxn = bf(qdq(dgu, g_dgu) @ wgu_tq.T)
+    d_down = qdq(dy.T, g_dy) @ qdq(h.T, g_h).T
+    d_gu = qdq(dgu.T, g_dgu) @ qdq(xn.T, g_xn).T
+    mean = (dxn * xn).sum(1, keepdim=True) / d
+    dx = bf(inv[:, None] * (dxn - xn * mean) + dy)
+    for p, w, (m, v), gr in zip(params, master, mom, (d_gu, d_down)):   # AdamW, torch.optim.AdamW order
+        w.mul_(1.0)
+        m.lerp_(gr, 0.1)
+        v.mul_(0.95).addcmul_(gr, gr, value=0.05)
+        w.addcdiv_(m, v.sqrt().div_(math.sqrt(0.05)).add_(1e-8), value=-1e-4 / 0.1)
+        p.copy_(bf(w))
+    dt = time.perf_counter() - t0
+    pool.shutdown()
+    assert torch.isfinite(y).all() and torch.isfinite(dx).all()
+    return tokens / dt, cores, dt
 
 
 def reference_arm(args, world, rank):
+    """The reference's own CPU path restated (the oracle: quantize,
+    dequantize, fp32 matmul; float4utils.py:79-148 and the emulation of
+    cutlass_mm_fp4.cu:182-184) on the host cores, one [256 x 2048] tile of the
+    8192^3 GEMM per step.  Rank 0 only."""
     if world > 1 and rank != 0:
         return None
-    tflops, cores, dt, _ = cpu_gemm_sample()
-    steps = []
     for _ in range(args.warmup):
         cpu_gemm_sample()
+    vals, secs = [], []
+    cores = 1
     for _ in range(args.steps):
-        v, _, dt, _ = cpu_gemm_sample()
-        steps.append(v)
-    val = statistics.median(steps)
-    sample = "256 of 8192 rows of the 8192^3 GEMM: oracle dequantize + torch fp32 matmul on host cores"
+        v, cores, dt, _ = cpu_gemm_sample()
+        vals.append(v)
+        secs.append(dt)
+    val = statistics.median(vals)
+    flops_tile = 2.0 * CPU_GEMM_ROWS * CPU_GEMM_COLS * 8192
+    sample = (f"{CPU_GEMM_ROWS} x {CPU_GEMM_COLS} output tile of the 8192^3 GEMM per step ({flops_tile:.3g} flop): "
+              f"oracle quantize (global scales) + dequantize of both operand slices + torch fp32 matmul on {cores} "
+              "host threads")
     return {"impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 2.0 * 8192 ** 3 / (val * 1e12) * 1e3,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.mean(secs) * 1e3,
+            "ms_per_full_8192_cubed_extrapolated": 2.0 * 8192 ** 3 / (val * 1e12) * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "NVFP4 block-scaled GEMM M=N=K=8192 (seed 1), CPU emulation sample",
+            "config": {"workload": "NVFP4 block-scaled GEMM M=N=K=8192 (seed 1), CPU emulation of one "
+                                   f"{CPU_GEMM_ROWS} x {CPU_GEMM_COLS} output tile per step",
                        "global_batch": 8192, "seq_len": 1, "parallelism": "rank0 host cores"},
             "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -735,16 +860,32 @@ def main(argv=None):
         line["mxfp4_gemm_8192"] = gemm["mxfp4"]
     if "cublaslt_error" in gemm:
         line["cublaslt_error"] = gemm["cublaslt_error"]
-    if rank == 0 and world == 1 and "cpu" not in skip:
+    cpu = rank == 0 and world == 1 and "cpu" not in skip
+    if cpu:
         v, cores, dt, _ = cpu_gemm_sample()
         line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                                "sample": "256 of 8192 rows of the 8192^3 GEMM: oracle dequantize + torch fp32 "
-                                          f"matmul on {cores} host threads ({dt:.2f} s)"}
+                                "sample": f"{CPU_GEMM_ROWS} x {CPU_GEMM_COLS} output tile of the 8192^3 GEMM: oracle "
+                                          "quantize + dequantize of both operand slices + torch fp32 matmul on "
+                                          f"{cores} host threads ({dt:.2f} s)"}
     if world == 1 and "quant" not in skip:
         line["quant"] = bench_quant(pkg, args, peaks)
+        if cpu:
+            v, cores, dt = cpu_quant_sample()
+            line["quant"]["cpu_baseline"] = {
+                "value": v, "unit": "GB/s", "cores": cores, "kind": "port",
+                "sample": f"2048 of 32768 rows: oracle 1/RMS, amax of (x*inv_rms)*gamma and NVFP4 quantize on "
+                          f"{cores} host threads ({dt:.2f} s), GB/s of the rows' algorithmic bytes"}
     if world == 1 and "mlp_block" not in skip:
         line["mlp_block"] = bench_mlp(pkg, args, world, rank, 1, 4096, 14336, 16384, seed=3, e2e_steps=args.steps)
         line["mlp_block"]["workload"] = "1 RMSNorm+SwiGLU block, 16384 tokens, d=4096, ff=14336, AdamW fp32"
+        if cpu:
+            v, cores, dt = cpu_mlp_sample()
+            line["mlp_block"]["cpu_baseline"] = {
+                "value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                "sample": f"one block step at 128 tokens (d 4096, ff 14336): oracle quantize/dequantize of every "
+                          f"GEMM operand incl. both weight orientations, torch fp32 matmuls, AdamW on {cores} host "
+                          f"threads ({dt:.2f} s); tokens/s = 128 / that time (the per-step weight work does not "
+                          "shrink with tokens, so this understates the CPU rate at 16384 tokens)"}
     if "mlp_stack" not in skip:
         line["mlp_stack"] = bench_mlp(pkg, args, world, rank, 8, 8192, 28672, 65536, seed=4, pg=pg)
         line["mlp_stack"]["workload"] = ("8 RMSNorm+SwiGLU blocks, d=8192, ff=28672, 65536 global tokens split "

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define NVFP4B200_API_VERSION 3
+#define NVFP4B200_API_VERSION 4
 
 enum nvfp4b200_status {
   NVFP4B200_OK = 0,
@@ -155,10 +155,11 @@ int nvfp4b200_global_scale(const void* x, int64_t n, uint32_t* ws, float* global
  * counterpart in the reference.  Allocates nothing: its scratch is a fixed
  * ~16 KB array inside the library's device memory, held by every GPU that
  * loads the library until the process exits.  Limit: n <= 2^30 elements
- * (larger n returns NVFP4B200_ERR_BAD_SHAPE).  The first call on a device
- * looks up the array's device address (make that first call before any
- * stream capture).  All calls share the array: calls that overlap on the
- * GPU race. */
+ * (larger n returns NVFP4B200_ERR_BAD_SHAPE).  Every call looks up the
+ * array's device address in the current context, so a cudaDeviceReset
+ * between calls is safe; the first call on a device may load the library's
+ * device code for that device (make it before any stream capture).  All
+ * calls share the array: calls that overlap on the GPU race. */
 int nvfp4b200_global_scale_noalloc(const void* x, int64_t n, float* global_scale_out, float* amax_out,
                                    void* stream);
 
@@ -237,14 +238,32 @@ int nvfp4b200_rmsnorm_bwd(const void* x, const void* gamma, const float* inv_rms
 /* Element-wise y = a + b over n bf16 elements (residual add). */
 int nvfp4b200_add_bf16(const void* a, const void* b, void* y, int64_t n, void* stream);
 
-/* AdamW on a bf16 parameter with fp32 moments:
+/* AdamW on a bf16 parameter with fp32 moments (no master copy):
  * g = grad * grad_scale (grad bf16 or fp32 per grad_dtype);
- * m = b1*m + (1-b1)*g; v = b2*v + (1-b2)*g^2;
- * p = p - lr*((m/bc1)/(sqrt(v/bc2)+eps) + wd*p), rounded to bf16. */
+ * m = b1*m + (1-b1)*g; v = b2*v + (1-b2)*(g*g);
+ * p = p - lr*((m/bc1)/(sqrt(v/bc2)+eps) + wd*p), rounded to bf16.
+ * Every operation is rounded once in this order.  An update below half a
+ * bf16 ulp of p is lost; nvfp4b200_adamw_master_step keeps it. */
 int nvfp4b200_adamw_step(void* param, const void* grad, int grad_dtype, float* m, float* v,
                          int64_t n, float lr, float beta1, float beta2, float eps,
                          float weight_decay, float bias_corr1, float bias_corr2,
                          float grad_scale, void* stream);
+
+/* AdamW with an fp32 master copy of a bf16 parameter (no counterpart in the
+ * reference, which trains with torch's optimizers): master, m and v are fp32
+ * [n]; param (bf16 [n]) is overwritten with bf16(master) after the update.
+ * The order of operations is torch.optim.AdamW's, each rounded once:
+ *   g = grad * grad_scale;  w = w * one_minus_lr_wd;
+ *   m = m + one_minus_beta1 * (g - m);  v = beta2*v + one_minus_beta2*(g*g);
+ *   w = w - step_size * (m / (sqrt(v)/bias_corr2_sqrt + eps))
+ * with one_minus_lr_wd = 1 - lr*wd, step_size = lr / (1 - beta1^t) and
+ * bias_corr2_sqrt = sqrt(1 - beta2^t) computed by the caller.  Updates below
+ * half a bf16 ulp of the parameter accumulate in the master instead of
+ * being rounded away. */
+int nvfp4b200_adamw_master_step(void* param, float* master, const void* grad, int grad_dtype, float* m, float* v,
+                                int64_t n, float one_minus_lr_wd, float one_minus_beta1, float beta2,
+                                float one_minus_beta2, float eps, float step_size, float bias_corr2_sqrt,
+                                float grad_scale, void* stream);
 
 #ifdef __cplusplus
 }

@@ -46,6 +46,8 @@ SIGNATURES = {
     "nvfp4b200_rmsnorm_bwd": [c_void_p] * 7 + [c_i64, c_i64, c_void_p],
     "nvfp4b200_add_bf16": [c_void_p, c_void_p, c_void_p, c_i64, c_void_p],
     "nvfp4b200_adamw_step": [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_i64] + [c_float] * 8 + [c_void_p],
+    "nvfp4b200_adamw_master_step": [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_i64] + [c_float] * 8
+                                   + [c_void_p],
 }
 
 _lock = threading.Lock()

