@@ -330,10 +330,17 @@ def bench_gemm(pkg, args, world, rank, peaks):
     e2e_ms = max_over_ranks(pipelined_e2e(args.steps, upload, compute, download), world)
     out = dev[(args.steps - 1) % 2][4]
     h2d = qa.numel() + qb.numel() + sa.numel() + sb.numel()
+    d2h = out.numel() * 2
+    bw_in, bw_out = pcie_bandwidth(hout[0], dev[0][4])
+    # with both directions overlapped, a step cannot be shorter than the slower direction's copy
+    pcie_ms = max(h2d / (bw_in * 1e9), d2h / (bw_out * 1e9)) * 1e3
     res["e2e"] = {"value": world * flops * args.steps / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                  "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out.numel() * 2,
+                  "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                   "path": "nvfp4b200_nvfp4_mm C ABI (gn_kernels::cutlass_sm120a_nvfp4_mm contract)",
-                  "pipeline": PIPELINE_NOTE}
+                  "pipeline": PIPELINE_NOTE,
+                  "pcie": {"h2d_gbps": bw_in, "d2h_gbps": bw_out, "bound_ms_per_step": pcie_ms,
+                           "bound_tflops": world * flops / (pcie_ms * 1e-3) / 1e12,
+                           "note": "pinned-copy bandwidth measured here; the e2e ceiling is the slower direction"}}
     # correctness spot check against float64 (a few elements)
     res["spot_check_max_rel_err"] = gemm_spot_check(qa, sa, qb, sb, out, ga, gb)
     # M sweep at N = K = 8192 (same B operand), ours and cuBLASLt, L2 flushed per launch
@@ -453,7 +460,8 @@ def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=No
     from nvfp4_b200.mlp import NVFP4MLPStackTrainer
     t_local = global_tokens // world
     trainer = NVFP4MLPStackTrainer(n_blocks, d, f, device="cuda", seed=seed, micro_tokens=micro_tokens,
-                                   process_group=pg, max_local_tokens=t_local)
+                                   process_group=pg, max_local_tokens=t_local,
+                                   comm_sms=getattr(args, "comm_sms", 0), zero=not getattr(args, "allreduce", False))
     g = torch.Generator(device="cuda").manual_seed(seed * 1000 + rank)
     x = torch.randn(t_local, d, device="cuda", generator=g).to(torch.bfloat16)
     dy = (torch.randn(t_local, d, device="cuda", generator=g) * 1e-3).to(torch.bfloat16)
@@ -476,6 +484,10 @@ def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=No
     res = {"tokens_per_s": global_tokens / (ms * 1e-3), "ms_per_step": ms, "tflops": flops / (ms * 1e-3) / 1e12,
            "flops_per_step": flops, "n_gpus": world, "tokens_global": global_tokens, "tokens_per_rank": t_local,
            "micro_tokens": micro_tokens, "clocks": clk.summary(), "finite": bool(torch.isfinite(r).all().item())}
+    if world > 1:
+        res["exchange"] = ("ZeRO-1: reduce-scatter + sharded AdamW + all-gather" if trainer.opt is not None
+                           else "all-reduce + replicated AdamW")
+        res["comm_sms"] = trainer.comm_sms
     # e2e through the public API: pinned host tokens + upstream grad copied in, step result read back
     hx = x.cpu().pin_memory()
     hdy = dy.cpu().pin_memory()
@@ -500,11 +512,32 @@ def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=No
     res["e2e"] = {"value": global_tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
                   "h2d_bytes_per_step": 2 * x.numel() * 2 * world, "d2h_bytes_per_step": 4 * world,
                   "pipeline": PIPELINE_NOTE}
-    if getattr(args, "breakdown", False) and world == 1:
-        res["kernel_breakdown"] = step_breakdown(trainer, x, dy, n_blocks, d, f, micro_tokens)
+    if getattr(args, "breakdown", False):   # every rank runs the profiled step (it holds collectives)
+        bd = step_breakdown(trainer, x, dy, n_blocks, d, f, min(micro_tokens, t_local))
+        if world > 1:
+            bd["exposed_comm_ms_max_over_ranks"] = max_over_ranks(bd.get("exposed_comm_ms", 0.0), world)
+        res["kernel_breakdown"] = bd
     del trainer
     torch.cuda.empty_cache()
     return res
+
+
+def pcie_bandwidth(host_buf, dev_buf, reps: int = 5):
+    """Pinned host <-> device copy bandwidth (GB/s, best of `reps`) for
+    buffers of this size, H2D and D2H each alone."""
+    import torch
+    res = []
+    for fn in (lambda: dev_buf.copy_(host_buf, non_blocking=True), lambda: host_buf.copy_(dev_buf, non_blocking=True)):
+        best = float("inf")
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        res.append(host_buf.numel() * host_buf.element_size() / (best * 1e-3) / 1e9)
+    return res[0], res[1]
 
 
 PIPELINE_NOTE = ("every step uploads its inputs from pinned host memory and downloads its result inside the "
@@ -565,7 +598,10 @@ def step_breakdown(trainer, x, dy, n_blocks, d, f, micro):
     real overlap, outside every timed region): device time per kernel, and each
     NVFP4 GEMM launch attributed to its role by its place in the step's fixed
     launch order (per micro-batch: gate/up and down per block forward, then dh,
-    dW_down, dxn and dW_gu per block backward)."""
+    dW_down, dxn and dW_gu per block backward).  With a process group the
+    NCCL kernels are separated out: ``exposed_comm_ms`` is the step's span
+    minus the union of its compute-kernel intervals (time in which only
+    collectives run, or nothing)."""
     import collections
     import torch
     from torch.profiler import ProfilerActivity, profile
@@ -598,8 +634,23 @@ def step_breakdown(trainer, x, dy, n_blocks, d, f, micro):
         roles[r].append(ms)
     busy = sum(v[1] for v in agg.values())
     span = (ks[-1][1] - ks[0][0]) / 1e3
+    # collectives: time during which only NCCL kernels (or nothing) run, i.e. the
+    # span minus the union of all compute-kernel intervals
+    comp = sorted((a, b) for a, b, n in ks if "nccl" not in n.lower())
+    union, cur = 0.0, None
+    for a, b in comp:
+        if cur is None or a > cur[1]:
+            if cur is not None:
+                union += cur[1] - cur[0]
+            cur = [a, b]
+        else:
+            cur[1] = max(cur[1], b)
+    if cur is not None:
+        union += cur[1] - cur[0]
+    nccl_ms = sum((b - a) / 1e3 for a, b, n in ks if "nccl" in n.lower())
     return {
-        "span_ms": span, "kernel_busy_ms": busy, "launches": len(ks),
+        "span_ms": span, "kernel_busy_ms": busy, "launches": len(ks), "compute_busy_ms": union / 1e3,
+        "nccl_kernel_ms": nccl_ms, "exposed_comm_ms": span - union / 1e3,
         "kernels": [{"name": k, "launches": c, "ms": round(ms, 3), "share": round(ms / busy, 4)}
                     for k, (c, ms) in sorted(agg.items(), key=lambda kv: -kv[1][1])[:16]],
         "gemm_roles": {r: {"launches": len(v), "mean_ms": round(sum(v) / len(v), 4),
@@ -795,6 +846,10 @@ def main(argv=None):
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the GEMM M sweep")
     ap.add_argument("--no-clock-hold", action="store_true", help="skip the 1 s sustained clock window (profiling)")
+    ap.add_argument("--comm-sms", type=int, default=0,
+                    help="MLP stack at N > 1: SMs left free of GEMMs for the NCCL kernels (0 = none)")
+    ap.add_argument("--allreduce", action="store_true",
+                    help="MLP stack at N > 1: plain all-reduce + replicated AdamW instead of ZeRO-1")
     ap.add_argument("--breakdown", action="store_true",
                     help="after the timed MLP steps, one more step under torch.profiler: per-kernel device time")
     ap.add_argument("--only", choices=["gemm", "gemm_sweep", "quant", "mlp_block", "mlp_stack"], default=None,

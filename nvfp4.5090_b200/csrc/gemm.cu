@@ -87,9 +87,20 @@ constexpr int ACC1_COL = 192;                         // buffer 1 starts inside 
 constexpr int SF_COL = 448;                           // scale slot: A 4 x 4 columns, then B 4 x 8 columns
 constexpr int SF_COLS = 12 * KBLOCKS;
 static_assert(ACC1_COL + ACC_COLS <= SF_COL && SF_COL + SF_COLS <= TMEM_COLS, "TMEM columns");
-constexpr int NUM_BARS = 2 * STAGES + 3 + EPI_WARPS;  // full, empty, tmem_full, overlap_free, drain, epilogue loads
-constexpr int BAR_BYTES = 512;                        // mbarriers + TMEM address slot + abort flag
-static_assert(NUM_BARS * 8 + 8 <= BAR_BYTES, "barrier area");
+// Tile schedule: a cluster's first tile is its cluster id; every further
+// tile is claimed from a per-launch counter in global memory (dynamic
+// scheduling: clusters that start late, for example behind a collective
+// kernel holding some SMs, simply claim fewer tiles).  The leader CTA's
+// producer warp claims tile ids and publishes them, through a ring of
+// TILE_RING slots in both CTAs' shared memory, to every warp of the pair that
+// walks tiles; -1 ends the walk.
+constexpr int TILE_RING = 4;
+// readers of every ring slot: leader MMA warp + 8 epilogue warps, peer producer + 8 epilogue warps
+constexpr int RING_READERS = 2 * (1 + EPI_WARPS);
+constexpr int SCHED_SLOTS = 256;                      // per-launch tile counters, used round robin
+constexpr int NUM_BARS = 2 * STAGES + 3 + EPI_WARPS + 2 * TILE_RING;  // + ring full / empty
+constexpr int BAR_BYTES = 512;                        // mbarriers + TMEM address slot + abort flag + tile ring
+static_assert(NUM_BARS * 8 + 8 + 4 * TILE_RING <= BAR_BYTES, "barrier area");
 constexpr int OUT_CHUNK_BYTES = 32 * 128;             // one epilogue warp's 32 rows x 64 bf16 output chunk
 constexpr int OUT_BYTES = EPI_WARPS * OUT_CHUNK_BYTES;  // bf16 output staging for the TMA stores
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024 + BAR_BYTES;  // + worst-case 1 KB alignment
@@ -131,7 +142,15 @@ struct Params {
   int stages;                // pipeline stages in use (STAGES, or DSW_STAGES with dswiglu)
   int out_bytes;             // epilogue staging bytes (OUT_BYTES or DSW_OUT_BYTES)
   int mx;                    // MXFP4 operands: 1x32 blocks, UE8M0 scales (kind::mxf4)
+  int sched_slot;            // this launch's tile counter: g_tile_sched[sched_slot]
 };
+
+// Per-launch tile counters: [0] tiles claimed beyond the first wave, [1]
+// clusters that have finished claiming.  The last cluster to finish resets
+// both to zero, so a slot is clean for the launch that reuses it (launches
+// take slots round robin).  Every wait in the kernel is bounded, so even a
+// launch that gives up reaches the reset.
+__device__ uint32_t g_tile_sched[SCHED_SLOTS][2];
 
 // ---------------------------------------------------------------------------
 // PTX wrappers
@@ -160,6 +179,14 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 // Arrive on a barrier of either CTA of the pair (address from mapa).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// Arrive with release semantics at cluster scope (orders this thread's prior
+// shared-memory accesses, local or remote, before the arrival).
+__device__ __forceinline__ void mbar_arrive_release_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+__device__ __forceinline__ void st_cluster_s32(uint32_t cluster_addr, int v) {
+  asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -456,6 +483,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + p.out_bytes);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* tile_ring = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();          // 0 = leader (issues the MMAs)
@@ -466,6 +494,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const uint32_t overlap_free_bar = smem_u32(bars + 2 * STAGES + 1);     // leader: shared columns drained
   const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 2);            // leader: error-path drain
   auto load_bar = [&](int w) { return smem_u32(bars + 2 * STAGES + 3 + w); };  // epilogue warp w's TMA loads
+  // tile ring: full (each CTA, one arrival from the leader's producer), empty (leader, RING_READERS arrivals)
+  auto ring_full = [&](int i) { return smem_u32(bars + 2 * STAGES + 3 + EPI_WARPS + i); };
+  auto ring_empty = [&](int i) { return smem_u32(bars + 2 * STAGES + 3 + EPI_WARPS + TILE_RING + i); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -476,6 +507,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     mbar_init(overlap_free_bar, 2 * EPI_WARPS);
     mbar_init(drain_bar, 1);
     for (int w = 0; w < EPI_WARPS; ++w) mbar_init(load_bar(w), 1);
+    for (int i = 0; i < TILE_RING; ++i) {
+      mbar_init(ring_full(i), 1);
+      mbar_init(ring_empty(i), RING_READERS);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tmap(&tmap_a);
@@ -499,13 +534,55 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
 
+  // The i-th tile id of this cluster, read from the ring by a whole warp (the
+  // slot is then released to the leader's producer).  -1: no more tiles.
+  // Returns false when the bounded wait gave up.
+  auto ring_read = [&](int i, int& tile) -> bool {
+    const int slot = i % TILE_RING;
+    if (!warp_wait<true>(ring_full(slot), (uint32_t)(i / TILE_RING) & 1u, abort_flag)) return false;
+    tile = tile_ring[slot];
+    __syncwarp();
+    if (lane == 0) mbar_arrive_release_cluster(map_to_rank(ring_empty(slot), 0));
+    return true;
+  };
+
   if (warp == 0) {
     // ---------------- TMA producer (both CTAs, whole warp; one lane issues) ----------------
     int stage = 0;
     uint32_t phase = 0;
     uint32_t armed = 0, armed_parity = 0;  // leader: stages whose barrier expects bytes, and the phase armed
     bool ok = true;
-    for (int tile = cluster_id; ok && tile < total_tiles; tile += num_clusters) {
+    uint32_t* sched = g_tile_sched[p.sched_slot];
+    int tile = cluster_id, next = -1;
+    for (int i = 0; ok; ++i) {
+      if (leader) {
+        // publish tile i in both CTAs' rings
+        const int slot = i % TILE_RING;
+        if (!warp_wait<true>(ring_empty(slot), ((uint32_t)(i / TILE_RING) & 1u) ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          tile_ring[slot] = tile;
+          st_cluster_s32(map_to_rank(smem_u32((const void*)(tile_ring + slot)), 1), tile);
+          mbar_arrive_release_cluster(map_to_rank(ring_full(slot), 0));
+          mbar_arrive_release_cluster(map_to_rank(ring_full(slot), 1));
+        }
+        __syncwarp();
+        if (tile < 0) break;
+        // claim the tile after this one now: the atomic's latency hides behind this tile's loads
+        if (lane == 0) {
+          const uint32_t c = atomicAdd(&sched[0], 1u);
+          next = c < (uint32_t)(total_tiles - num_clusters) ? num_clusters + (int)c : -1;
+        }
+        next = __shfl_sync(0xffffffffu, next, 0);
+      } else {
+        if (!ring_read(i, tile)) {
+          ok = false;
+          break;
+        }
+        if (tile < 0) break;
+      }
       int mb, nb;
       tile_coords(tile, p, mb, nb);
       const int a_row = mb * TILE_M + (int)rank * CTA_M;
@@ -535,6 +612,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           phase ^= 1;
         }
       }
+      tile = next;
+    }
+    if (leader && lane == 0) {
+      // this cluster claims no more tiles; the last cluster to get here resets the counters
+      if (atomicAdd(&sched[1], 1u) == (uint32_t)num_clusters - 1u) {
+        atomicExch(&sched[0], 0u);
+        atomicExch(&sched[1], 0u);
+      }
     }
     if (!ok && lane == 0) {
       raise_abort(abort_flag);
@@ -555,8 +640,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       bool ok = true, issued = false;
       const uint32_t sfa_t = tmem_base + SF_COL;
       const uint32_t sfb_t = sfa_t + 4 * KBLOCKS;
-      int it = 0;  // tiles of this cluster so far; buffer = it & 1
-      for (int tile = cluster_id; ok && tile < total_tiles; tile += num_clusters, ++it) {
+      for (int it = 0; ok; ++it) {   // it: tiles of this cluster so far; buffer = it & 1
+        int tile;
+        if (!ring_read(it, tile)) {
+          ok = false;
+          break;
+        }
+        if (tile < 0) break;
         // The previous tile's epilogue has drained the 64 columns its buffer
         // shares with this tile's buffer.  Every epilogue warp finished the tile
         // before it first, so this buffer's own previous use is drained too.
@@ -660,14 +750,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       ld_pending = true;
     };
-    bool ok = true;
     int it = 0;
-    if (cluster_id < total_tiles) {
+    int tile = -1, next_tile = -1;
+    bool ok = ring_read(0, tile);
+    if (ok && tile >= 0) {
       int mb0, nb0;
-      tile_coords(cluster_id, p, mb0, nb0);
+      tile_coords(tile, p, mb0, nb0);
       issue_loads(mb0, nb0, half == 1 ? 1 : 0);   // tile 0 uses buffer 0: half 1 drains chunk 1 first
     }
-    for (int tile = cluster_id; tile < total_tiles; tile += num_clusters, ++it) {
+    for (; ok && tile >= 0; tile = next_tile, ++it) {
       int mb, nb;
       tile_coords(tile, p, mb, nb);
       ok = __all_sync(0xffffffffu, mbar_wait(tmem_full_bar, (uint32_t)(it & 1), abort_flag));
@@ -745,10 +836,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         __syncwarp();
         if (r == 0) {
           issue_loads(mb, nb, c ^ 1);
-        } else if (tile + num_clusters < total_tiles) {
-          int mb2, nb2;
-          tile_coords(tile + num_clusters, p, mb2, nb2);
-          issue_loads(mb2, nb2, (((it + 1) & 1) == 0 && half == 1) ? 1 : 0);
+        } else {   // the next tile's first chunk goes out while this warp waits for its accumulator
+          if (!ring_read(it + 1, next_tile)) {
+            ok = false;
+            break;
+          }
+          if (next_tile >= 0) {
+            int mb2, nb2;
+            tile_coords(next_tile, p, mb2, nb2);
+            issue_loads(mb2, nb2, (((it + 1) & 1) == 0 && half == 1) ? 1 : 0);
+          }
         }
       }
       if (!ok) break;
@@ -773,8 +870,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const int half = (warp - 2) >> 2;        // accumulator columns [128*half, 128*half+128)
     const uint32_t leader_overlap_free = map_to_rank(overlap_free_bar, 0);
     const float alpha = (p.scale_a ? *p.scale_a : 1.0f) * (p.scale_b ? *p.scale_b : 1.0f);
-    int it = 0;
-    for (int tile = cluster_id; tile < total_tiles; tile += num_clusters, ++it) {
+    for (int it = 0;; ++it) {
+      int tile;
+      if (!ring_read(it, tile)) {
+        if (lane == 0) raise_abort(abort_flag);
+        break;
+      }
+      if (tile < 0) break;
       int mb, nb;
       tile_coords(tile, p, mb, nb);
       bool ok = mbar_wait(tmem_full_bar, (uint32_t)(it & 1), abort_flag);
@@ -1212,6 +1314,12 @@ static int run(const void* a, const void* b, const void* sfa, const void* sfb, c
   const int max_sms = g_gemm_max_sms.load(std::memory_order_relaxed);
   if (max_sms > 0) cap = std::max(1, std::min(cap, max_sms / 2));
   const int clusters = (int)std::min<int64_t>(tiles, cap);
+  {
+    static std::atomic<uint32_t> seq[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    p.sched_slot = (int)(seq[dev & 63].fetch_add(1u, std::memory_order_relaxed) % SCHED_SLOTS);
+  }
   if (cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
       cudaSuccess)
     return NVFP4B200_ERR_CUDA;
@@ -1243,6 +1351,10 @@ int nvfp4b200_get_device_error(int* out) {
   const int qe = take_quant_device_error();
   if (qe == NVFP4B200_ERR_CUDA) return qe;
   if (*out == 0) *out = qe;
+  if (*out != 0) {   // a launch gave up: make sure no tile counter is left dirty (the device is idle here)
+    static const uint32_t zeros[gemm::SCHED_SLOTS][2] = {};
+    if (cudaMemcpyToSymbol(gemm::g_tile_sched, zeros, sizeof(zeros)) != cudaSuccess) return NVFP4B200_ERR_CUDA;
+  }
   return NVFP4B200_OK;
 }
 
