@@ -648,9 +648,21 @@ def step_breakdown(trainer, x, dy, n_blocks, d, f, micro):
     if cur is not None:
         union += cur[1] - cur[0]
     nccl_ms = sum((b - a) / 1e3 for a, b, n in ks if "nccl" in n.lower())
+    # the largest gaps between compute kernels: where the step waits, and for what
+    t0 = ks[0][0]
+    comp_named = sorted((a, b, n) for a, b, n in ks if "nccl" not in n.lower())
+    gaps = []
+    end_prev = comp_named[0][1] if comp_named else 0.0
+    for a1, b1, n1 in comp_named[1:]:
+        if a1 - end_prev > 200.0:   # > 0.2 ms without compute
+            during = sorted({n.split("(")[0].split("<")[0] for a, b, n in ks if "nccl" in n.lower() and a < a1 and b > end_prev})
+            gaps.append({"at_ms": round((end_prev - t0) / 1e3, 3), "ms": round((a1 - end_prev) / 1e3, 3),
+                         "next_kernel": n1.split("(")[0][:60], "nccl_running": during})
+        end_prev = max(end_prev, b1)
+    gaps.sort(key=lambda g: -g["ms"])
     return {
         "span_ms": span, "kernel_busy_ms": busy, "launches": len(ks), "compute_busy_ms": union / 1e3,
-        "nccl_kernel_ms": nccl_ms, "exposed_comm_ms": span - union / 1e3,
+        "nccl_kernel_ms": nccl_ms, "exposed_comm_ms": span - union / 1e3, "largest_gaps": gaps[:8],
         "kernels": [{"name": k, "launches": c, "ms": round(ms, 3), "share": round(ms / busy, 4)}
                     for k, (c, ms) in sorted(agg.items(), key=lambda kv: -kv[1][1])[:16]],
         "gemm_roles": {r: {"launches": len(v), "mean_ms": round(sum(v) / len(v), 4),
