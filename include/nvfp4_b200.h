@@ -259,11 +259,21 @@ int nvfp4b200_adamw_step(void* param, const void* grad, int grad_dtype, float* m
  * with one_minus_lr_wd = 1 - lr*wd, step_size = lr / (1 - beta1^t) and
  * bias_corr2_sqrt = sqrt(1 - beta2^t) computed by the caller.  Updates below
  * half a bf16 ulp of the parameter accumulate in the master instead of
- * being rounded away. */
+ * being rounded away.  amax_bits (device uint32, optional): the largest
+ * |bf16 parameter| written by this call, as float bits, combined into
+ * *amax_bits with an atomic max (zero it before the first call; NaN is
+ * ignored).  It lets the weights' global scale for the next quantization be
+ * taken from the update itself instead of another pass over the weights. */
 int nvfp4b200_adamw_master_step(void* param, float* master, const void* grad, int grad_dtype, float* m, float* v,
                                 int64_t n, float one_minus_lr_wd, float one_minus_beta1, float beta2,
                                 float one_minus_beta2, float eps, float step_size, float bias_corr2_sqrt,
-                                float grad_scale, void* stream);
+                                float grad_scale, uint32_t* amax_bits, void* stream);
+
+/* Global scales from amaxes (no reference counterpart): for i < n,
+ * global_scale_out[i] = amax_i/(6*448), amax_i = float bits amax_bits[i],
+ * and 1.0 when that amax is 0 or not finite -- exactly what
+ * nvfp4b200_global_scale computes from the tensor.  n <= 2^20. */
+int nvfp4b200_global_scale_from_amax(const uint32_t* amax_bits, float* global_scale_out, int64_t n, void* stream);
 
 #ifdef __cplusplus
 }

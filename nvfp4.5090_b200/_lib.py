@@ -47,7 +47,8 @@ SIGNATURES = {
     "nvfp4b200_add_bf16": [c_void_p, c_void_p, c_void_p, c_i64, c_void_p],
     "nvfp4b200_adamw_step": [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_i64] + [c_float] * 8 + [c_void_p],
     "nvfp4b200_adamw_master_step": [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_i64] + [c_float] * 8
-                                   + [c_void_p],
+                                   + [c_void_p, c_void_p],
+    "nvfp4b200_global_scale_from_amax": [c_void_p, c_void_p, c_i64, c_void_p],
 }
 
 _lock = threading.Lock()

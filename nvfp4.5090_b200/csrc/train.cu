@@ -348,11 +348,19 @@ __global__ void __launch_bounds__(256) adamw_kernel(uint16_t* __restrict__ p, co
 // fp32 master weights: w, m, v are updated in fp32 and the bf16 parameter is
 // written as round-to-nearest-even of the new w.  Updates smaller than half a
 // bf16 ulp of the parameter accumulate in w instead of being rounded away.
+// |bf16| of a packed pair as float bits (the larger one), NaN ignored
+__device__ __forceinline__ uint32_t absmax_pair_bits(uint32_t w) { return absmax_word_bits(w); }
+
+// amax_bits (optional): max |bf16 parameter| written by this launch, as float
+// bits, combined into *amax_bits with atomicMax (the caller zeroes it first);
+// NaN is ignored, as in the global-scale kernels.
 template <bool GRAD_F32>
 __global__ void __launch_bounds__(256) adamw_master_kernel(uint16_t* __restrict__ p, float* __restrict__ w,
                                                            const void* __restrict__ grad, float* __restrict__ m,
-                                                           float* __restrict__ v, int64_t n, MasterArgs a) {
+                                                           float* __restrict__ v, int64_t n, MasterArgs a,
+                                                           uint32_t* __restrict__ amax_bits) {
   const int64_t nv = n / 8;
+  uint32_t am = 0;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
     float g[8], mm[8], vv[8], ww[8];
     load_grad8(grad, i, GRAD_F32, g);
@@ -361,7 +369,10 @@ __global__ void __launch_bounds__(256) adamw_master_kernel(uint16_t* __restrict_
     load_f32x8(w, i, ww);
 #pragma unroll
     for (int j = 0; j < 8; ++j) ww[j] = adam_master_one(ww[j], g[j], mm[j], vv[j], a);
-    reinterpret_cast<uint4*>(p)[i] = make_uint4(pack2(ww[0], ww[1]), pack2(ww[2], ww[3]), pack2(ww[4], ww[5]), pack2(ww[6], ww[7]));
+    const uint4 pv = make_uint4(pack2(ww[0], ww[1]), pack2(ww[2], ww[3]), pack2(ww[4], ww[5]), pack2(ww[6], ww[7]));
+    reinterpret_cast<uint4*>(p)[i] = pv;
+    am = max(am, max(max(absmax_pair_bits(pv.x), absmax_pair_bits(pv.y)),
+                     max(absmax_pair_bits(pv.z), absmax_pair_bits(pv.w))));
     store_f32x8(w, i, ww);
     store_f32x8(m, i, mm);
     store_f32x8(v, i, vv);
@@ -372,8 +383,22 @@ __global__ void __launch_bounds__(256) adamw_master_kernel(uint16_t* __restrict_
     m[i] = mm;
     v[i] = vv;
     w[i] = r;
-    p[i] = bf16_bits_rn(r);
+    const uint16_t b = bf16_bits_rn(r);
+    p[i] = b;
+    am = max(am, absmax_pair_bits((uint32_t)b));
   }
+  if (amax_bits) {
+    am = __reduce_max_sync(0xffffffffu, am);
+    if ((threadIdx.x & 31) == 0 && am) atomicMax(amax_bits, am);
+  }
+}
+
+// g_i = amax_i / (6 * 448) from float bits (1 when the amax is 0 or not finite)
+__global__ void global_scale_from_amax_kernel(const uint32_t* __restrict__ amax_bits, float* __restrict__ g, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float amax = __uint_as_float(amax_bits[i]);
+  g[i] = (amax > 0.0f && amax <= 3.402823466e38f) ? __fdiv_rn(amax, 2688.0f) : 1.0f;
 }
 
 }  // namespace nvfp4b200
@@ -474,8 +499,9 @@ int nvfp4b200_adamw_step(void* param, const void* grad, int grad_dtype, float* m
 int nvfp4b200_adamw_master_step(void* param, float* master, const void* grad, int grad_dtype, float* m, float* v,
                                 int64_t n, float one_minus_lr_wd, float one_minus_beta1, float beta2,
                                 float one_minus_beta2, float eps, float step_size, float bias_corr2_sqrt,
-                                float grad_scale, void* stream) {
+                                float grad_scale, uint32_t* amax_bits, void* stream) {
   if (!param || !master || !grad || !m || !v) return NVFP4B200_ERR_INVALID_ARG;
+  if (amax_bits && !aligned(amax_bits, 4)) return NVFP4B200_ERR_MISALIGNED;
   if (grad_dtype != NVFP4B200_BF16 && grad_dtype != NVFP4B200_F32) return NVFP4B200_ERR_INVALID_ARG;
   if (n < 0) return NVFP4B200_ERR_BAD_SHAPE;
   if (!aligned(param, 16) || !aligned(master, 16) || !aligned(grad, 16) || !aligned(m, 16) || !aligned(v, 16))
@@ -487,9 +513,21 @@ int nvfp4b200_adamw_master_step(void* param, float* master, const void* grad, in
   const unsigned grid = grid_for(n / 8 + 1, 256);
   auto P = static_cast<uint16_t*>(param);
   if (grad_dtype == NVFP4B200_F32)
-    adamw_master_kernel<true><<<grid, 256, 0, (cudaStream_t)stream>>>(P, master, grad, m, v, n, a);
+    adamw_master_kernel<true><<<grid, 256, 0, (cudaStream_t)stream>>>(P, master, grad, m, v, n, a, amax_bits);
   else
-    adamw_master_kernel<false><<<grid, 256, 0, (cudaStream_t)stream>>>(P, master, grad, m, v, n, a);
+    adamw_master_kernel<false><<<grid, 256, 0, (cudaStream_t)stream>>>(P, master, grad, m, v, n, a, amax_bits);
+  return launch_status();
+}
+
+int nvfp4b200_global_scale_from_amax(const uint32_t* amax_bits, float* global_scale_out, int64_t n, void* stream) {
+  if (!amax_bits || !global_scale_out) return NVFP4B200_ERR_INVALID_ARG;
+  if (n < 0 || n > (1 << 20)) return NVFP4B200_ERR_BAD_SHAPE;
+  if (!aligned(amax_bits, 4) || !aligned(global_scale_out, 4)) return NVFP4B200_ERR_MISALIGNED;
+  int rc = check_device();
+  if (rc) return rc;
+  if (n == 0) return NVFP4B200_OK;
+  global_scale_from_amax_kernel<<<(unsigned)ceil_div(n, (int64_t)256), 256, 0, (cudaStream_t)stream>>>(
+      amax_bits, global_scale_out, (int)n);
   return launch_status();
 }
 

@@ -61,9 +61,13 @@ class QWeights:
     s_down_t: torch.Tensor
 
 
-def quantize_weights(w_gu: torch.Tensor, w_down: torch.Tensor, need_t: bool = True) -> QWeights:
-    g_gu = ops.global_scale(w_gu)
-    g_down = ops.global_scale(w_down)
+def quantize_weights(w_gu: torch.Tensor, w_down: torch.Tensor, need_t: bool = True,
+                     g_gu: Optional[torch.Tensor] = None, g_down: Optional[torch.Tensor] = None) -> QWeights:
+    """Both NVFP4 orientations of a block's weights.  The global scales are
+    computed here unless given (the trainer takes them from the previous
+    AdamW update, which already saw every weight it wrote)."""
+    g_gu = ops.global_scale(w_gu) if g_gu is None else g_gu
+    g_down = ops.global_scale(w_down) if g_down is None else g_down
     q_gu, s_gu = ops.quantize(w_gu, global_scale=g_gu)
     q_down, s_down = ops.quantize(w_down, global_scale=g_down)
     if need_t:
@@ -301,6 +305,11 @@ class NVFP4MLPStackTrainer:
             if world > 1:
                 self.reducer = BucketAllReducer(process_group)
         self.step_count = 0
+        # the weights' global scales for the next step, from the amaxes the AdamW
+        # update records while writing the weights ([block, (W_gu, W_down)]); None
+        # until the first update (then they are computed from the weights)
+        self.w_amax = torch.zeros(n_blocks, 2, device=self.device, dtype=torch.int32)
+        self.w_g: Optional[torch.Tensor] = None
         # W_gu rows interleave gate/up in blocks of 128 (fused SwiGLU epilogue) when F allows
         self.interleave = 128 if d_ff % 128 == 0 else 0
         # SMs left to the gradient collectives while the step's GEMMs run (DP only)
@@ -329,7 +338,9 @@ class NVFP4MLPStackTrainer:
                 if self.opt is not None:
                     self.opt.wait_params(bi)
                 b = self.blocks[bi]
-                qws[bi] = quantize_weights(b.w_gu, b.w_down, need_t=True)
+                g = self.w_g
+                qws[bi] = quantize_weights(b.w_gu, b.w_down, need_t=True, g_gu=None if g is None else g[bi, 0:1],
+                                           g_down=None if g is None else g[bi, 1:2])
             return qws[bi]
 
         for b in self.blocks:
@@ -354,12 +365,13 @@ class NVFP4MLPStackTrainer:
                     # the first micro-batch writes the fp32 accumulators, later ones add to them
                     g = block_backward(g, b.gamma, qws[bi], saved[bi], b.grad_gamma32, b.acc_gu, b.acc_down,
                                        accumulate=mi > 0, interleave=self.interleave)
-                    if last:
+                    if last and self.world > 1:   # the bf16 bucket is only needed for the exchange
                         b.grad_gu.copy_(b.acc_gu)
                         b.grad_down.copy_(b.acc_down)
                 saved[bi] = None
-                if last:
+                if last and (self.world > 1 or n_micro == 1):
                     b.grad[:self.d].copy_(b.grad_gamma32)
+                if last:
                     if self.opt is not None:
                         self.opt.reduce_scatter(bi, b.grad)
                     elif self.reducer is not None:
@@ -367,23 +379,62 @@ class NVFP4MLPStackTrainer:
         self.step_count += 1
         a = self.adam
 
-        def adamw(p, g, m, v, w=None):
+        def adamw(p, g, m, v, w=None, amax=None):
             kw = dict(lr=a.lr, beta1=a.beta1, beta2=a.beta2, eps=a.eps, weight_decay=a.weight_decay,
                       step=self.step_count, grad_scale=1.0 / self.world)
             if w is not None:
-                ops.adamw_master_step(p, w, g, m, v, **kw)
+                ops.adamw_master_step(p, w, g, m, v, amax_bits=amax, **kw)
             else:
                 ops.adamw_step(p, g, m, v, **kw)
+
+        d, ngu = self.d, 2 * self.f * self.d
+        n_real = d + ngu + self.d * self.f
+        # segments of a block's flat bucket and where each one's amax goes (gamma is not quantized)
+        seg_of = lambda bi: ((0, d, None), (d, d + ngu, self.w_amax[bi, 0:1]),
+                             (d + ngu, n_real, self.w_amax[bi, 1:2]))
+        track = a.master_weights
+        if track:
+            self.w_amax.zero_()
+
+        def shard_update(bi):
+            """update_fn of the ZeRO-1 optimizer for block bi: AdamW on the shard,
+            split at the segment boundaries it crosses (the padding past the
+            real parameters is updated as one more segment, without an amax)."""
+            sl = self.opt.shard_slice(bi)
+
+            def fn(p, g, m, v, w=None):
+                lo0 = sl.start
+                cuts = [(lo, hi, am) for lo, hi, am in seg_of(bi)] + [(n_real, sl.stop, None)]
+                for lo, hi, am in cuts:
+                    lo, hi = max(lo, sl.start), min(hi, sl.stop)
+                    if lo < hi:
+                        r = slice(lo - lo0, hi - lo0)
+                        adamw(p[r], g[r], m[r], v[r], None if w is None else w[r], am if track else None)
+            return fn
 
         # buckets were launched from the last block down: update in that order
         for bi in reversed(range(self.n_blocks)):
             b = self.blocks[bi]
             if self.opt is not None:
-                self.opt.update(bi, b.param, adamw, gather=False)
+                self.opt.update(bi, b.param, shard_update(bi), gather=False)
             else:
                 if self.reducer is not None:
                     self.reducer.wait(bi)
-                adamw(b.param, b.grad, b.m, b.v, b.master)
+                if self.world == 1 and n_micro > 1:
+                    # one rank, micro-batched: AdamW reads the fp32 accumulators directly
+                    # (no bf16 copy of the gradient)
+                    grads = (b.grad_gamma32, b.acc_gu.view(-1), b.acc_down.view(-1))
+                else:
+                    grads = tuple(b.grad[lo:hi] for lo, hi, _ in seg_of(bi))
+                for (lo, hi, am), g in zip(seg_of(bi), grads):
+                    adamw(b.param[lo:hi], g, b.m[lo:hi], b.v[lo:hi], None if b.master is None else b.master[lo:hi],
+                          am if track else None)
+        if track:
+            if self.opt is not None:
+                # each rank saw its shard of every weight: the global amax is the max over ranks
+                import torch.distributed as dist
+                dist.all_reduce(self.w_amax, op=dist.ReduceOp.MAX, group=self.pg)
+            self.w_g = ops.global_scale_from_amax(self.w_amax)
         if self.opt is not None:
             # gathers in the order the next forward uses the blocks: block 0 lands first
             for bi, b in enumerate(self.blocks):

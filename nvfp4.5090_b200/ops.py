@@ -361,9 +361,11 @@ def adamw_step(param: torch.Tensor, grad: torch.Tensor, m: torch.Tensor, v: torc
 
 def adamw_master_step(param: torch.Tensor, master: torch.Tensor, grad: torch.Tensor, m: torch.Tensor,
                       v: torch.Tensor, *, lr: float, beta1: float, beta2: float, eps: float, weight_decay: float,
-                      step: int, grad_scale: float = 1.0) -> None:
+                      step: int, grad_scale: float = 1.0, amax_bits: Optional[torch.Tensor] = None) -> None:
     """AdamW on an fp32 master copy (torch.optim.AdamW's operation order);
-    the bf16 ``param`` receives bf16(master) after the update."""
+    the bf16 ``param`` receives bf16(master) after the update.  ``amax_bits``
+    (a 1-element int32 CUDA tensor, zeroed by the caller) collects the
+    largest |bf16 parameter| written, as float bits (atomic max)."""
     _require(param.dtype == torch.bfloat16 and master.dtype == torch.float32 and m.dtype == torch.float32
              and v.dtype == torch.float32, "AdamW: bf16 parameter, fp32 master and moments")
     _require(grad.dtype in (torch.bfloat16, torch.float32), "AdamW: bf16 or fp32 gradient")
@@ -372,7 +374,19 @@ def adamw_master_step(param: torch.Tensor, master: torch.Tensor, grad: torch.Ten
              "AdamW: parameter, master, gradient and moments must have the same length")
     _lib.call("nvfp4b200_adamw_master_step", param.data_ptr(), master.data_ptr(), grad.data_ptr(),
               _DT_BF16 if grad.dtype == torch.bfloat16 else _DT_F32, m.data_ptr(), v.data_ptr(), n,
-              *adamw_master_scalars(lr, beta1, beta2, eps, weight_decay, step), grad_scale, _stream(param))
+              *adamw_master_scalars(lr, beta1, beta2, eps, weight_decay, step), grad_scale, _ptr(amax_bits),
+              _stream(param))
+
+
+def global_scale_from_amax(amax_bits: torch.Tensor) -> torch.Tensor:
+    """float32 global scales amax/(6*448) (1 for 0 or non-finite) from an int32
+    tensor of amax float bits; same shape."""
+    _require(amax_bits.is_cuda and amax_bits.dtype == torch.int32 and amax_bits.is_contiguous(),
+             "amax bits are a contiguous int32 CUDA tensor")
+    g = torch.empty(amax_bits.shape, device=amax_bits.device, dtype=torch.float32)
+    _lib.call("nvfp4b200_global_scale_from_amax", amax_bits.data_ptr(), g.data_ptr(), amax_bits.numel(),
+              _stream(amax_bits))
+    return g
 
 
 def adamw_master_scalars(lr: float, beta1: float, beta2: float, eps: float, weight_decay: float, step: int):

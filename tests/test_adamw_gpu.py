@@ -117,4 +117,26 @@ def test_trainer_keeps_master_weights(pkg):
     tr.step(x, dy)
     torch.cuda.synchronize()
     assert torch.equal(b.param.view(torch.int16), b.master.to(torch.bfloat16).view(torch.int16))
+    # the next step's weight global scales come from the update's amax: exactly the weights' own
+    assert torch.equal(tr.w_g[0, 0:1], pkg.ops.global_scale(b.w_gu))
+    assert torch.equal(tr.w_g[0, 1:2], pkg.ops.global_scale(b.w_down))
     assert pkg.ops.device_error() == 0
+
+
+def test_adamw_master_amax_and_scale_from_amax(pkg):
+    """The master kernel's amax output equals the max |bf16 parameter| it
+    wrote (odd length: vector body and scalar tail, the maximum in the tail),
+    and nvfp4b200_global_scale_from_amax reproduces nvfp4b200_global_scale."""
+    n = 1000 + 3
+    gen = torch.Generator(device="cuda").manual_seed(33)
+    w = torch.randn(n, device="cuda", generator=gen)
+    w[-2] = -7.5
+    p = w.to(torch.bfloat16)
+    m, v = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+    g = (0.1 * torch.randn(n, device="cuda", generator=gen)).to(torch.bfloat16)
+    amax = torch.zeros(1, device="cuda", dtype=torch.int32)
+    pkg.ops.adamw_master_step(p, w, g, m, v, step=1, amax_bits=amax, **HP)
+    torch.cuda.synchronize()
+    assert amax.view(torch.float32).item() == p.float().abs().max().item()
+    gs = pkg.ops.global_scale_from_amax(torch.stack([amax[0], torch.zeros_like(amax[0])]))
+    assert gs[0].item() == pkg.ops.global_scale(p).item() and gs[1].item() == 1.0

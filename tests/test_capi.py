@@ -81,11 +81,15 @@ MIS = FAKE + 4
     (lambda L: L.nvfp4b200_mxfp4_mm(None, FAKE, FAKE, FAKE, None, FAKE, 8, 8, 64, None), 1),                                  # limit out of range
     (lambda L: L.nvfp4b200_adamw_step(FAKE, FAKE, 5, FAKE, FAKE, 8, 1e-3, .9, .95, 1e-8, 0., 1., 1., 1., None), 1),
     (lambda L: L.nvfp4b200_adamw_master_step(FAKE, None, FAKE, 0, FAKE, FAKE, 8, 1., .1, .95, .05, 1e-8, 1e-3, 1.,
-                                             1., None), 1),                                # no master
+                                             1., None, None), 1),                          # no master
     (lambda L: L.nvfp4b200_adamw_master_step(FAKE, MIS, FAKE, 0, FAKE, FAKE, 8, 1., .1, .95, .05, 1e-8, 1e-3, 1.,
-                                             1., None), 3),                                # misaligned master
+                                             1., None, None), 3),                          # misaligned master
     (lambda L: L.nvfp4b200_adamw_master_step(FAKE, FAKE, FAKE, 0, FAKE, FAKE, -1, 1., .1, .95, .05, 1e-8, 1e-3,
-                                             1., 1., None), 2),
+                                             1., 1., None, None), 2),
+    (lambda L: L.nvfp4b200_adamw_master_step(FAKE, FAKE, FAKE, 0, FAKE, FAKE, 8, 1., .1, .95, .05, 1e-8, 1e-3,
+                                             1., 1., FAKE + 2, None), 3),                  # misaligned amax word
+    (lambda L: L.nvfp4b200_global_scale_from_amax(None, FAKE, 4, None), 1),
+    (lambda L: L.nvfp4b200_global_scale_from_amax(FAKE, FAKE, -1, None), 2),
 ])
 def test_argument_validation_without_device(pkg, call, expected):
     assert call(pkg._lib.load()) == expected

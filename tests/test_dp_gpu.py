@@ -81,6 +81,10 @@ def _worker(rank, world, port, zero, out_path):
                 full = torch.empty(w.numel() * world, device="cuda", dtype=torch.float32)
                 dist.all_gather_into_tensor(full, w)
                 masters.append(full[:b.numel].cpu())
+        # the weight global scales of the next step (shard amaxes, max over ranks) are the weights' own
+        for i, b in enumerate(tr.blocks):
+            assert torch.equal(tr.w_g[i, 0:1], sys.modules["nvfp4_b200"].ops.global_scale(b.w_gu))
+            assert torch.equal(tr.w_g[i, 1:2], sys.modules["nvfp4_b200"].ops.global_scale(b.w_down))
         if rank == 0:
             torch.save({"params": [b.param[:b.numel].cpu() for b in tr.blocks], "p0": [p.cpu() for p in p0],
                         "grads": None if grads is None else [g.cpu() for g in grads], "masters": masters,
@@ -111,7 +115,8 @@ def test_two_rank_trainer_matches_single_rank(pkg, tmp_path):
     for b, p0 in zip(single.blocks, res[False]["p0"]):
         assert torch.equal(b.param[:b.numel].cpu().view(torch.int16), p0.view(torch.int16))
     single.step(x, dy)
-    g1 = [b.grad[:b.numel].float().cpu() for b in single.blocks]
+    # one rank with two micro-batches: the gradient is the fp32 accumulators
+    g1 = [torch.cat([b.grad_gamma32, b.acc_gu.flatten(), b.acc_down.flatten()]).cpu() for b in single.blocks]
     single.step(x, dy)
     torch.cuda.synchronize()
     assert pkg.ops.device_error() == 0
