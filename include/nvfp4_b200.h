@@ -128,7 +128,9 @@ int nvfp4b200_rmsnorm_quant_nvfp4(const void* x, const void* gamma, void* q, voi
  * (1.0 when that amax is 0 or not finite).  `ws` is a caller-owned device
  * workspace of 2 uint32 that must be zero before the first call; every call
  * leaves it zero again.  Calls sharing one `ws` must not overlap.
- * k % 16 == 0 and k <= 8192. */
+ * k % 16 == 0 and k <= 16384.  The sum of squares is not reduced in the
+ * reference kernel's order (this path has none), so inv_rms may differ from
+ * nvfp4b200_rmsnorm_quant_nvfp4's by about one ulp. */
 int nvfp4b200_rmsnorm_stats(const void* x, const void* gamma, float* inv_rms,
                             int64_t rows, int64_t k, float eps,
                             uint32_t* ws, float* global_scale_out, void* stream);

@@ -280,24 +280,21 @@ __global__ void __launch_bounds__(RMS_WARPS * 32) rms_inv_stream_kernel(
 
 __device__ int g_quant_error = 0;
 
-template <int BPT, bool HAS_GAMMA, int MODE>
+template <int BPT, bool HAS_GAMMA>
 __global__ void __launch_bounds__(256) rmsnorm_cta_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma, uint8_t* __restrict__ q,
     uint8_t* __restrict__ s, float* __restrict__ inv_rms_out, int64_t rows, int64_t pad_rows, int64_t k,
-    int64_t pad_cols, float eps, const float* __restrict__ gptr, uint32_t* ws, float* g_out, int q8) {
+    int64_t pad_cols, float eps, const float* __restrict__ gptr, int q8) {
   __shared__ float warp_sum[8];
   __shared__ float row_inv;
   __shared__ float inv_tab[256];
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
   const int nwarps = blockDim.x >> 5;
   const int64_t nblk = k >> 4;
-  const int64_t cover = MODE == 0 ? pad_rows : rows;
-  float g = 1.0f, inv_g = 1.0f;
-  if (MODE == 0) {
-    g = load_global_scale(gptr);
-    inv_g = __frcp_rn(g);
-    fill_inv_scale_table(inv_tab, g);
-  }
+  const int64_t cover = pad_rows;
+  const float g = load_global_scale(gptr);
+  const float inv_g = __frcp_rn(g);
+  fill_inv_scale_table(inv_tab, g);
   uint64_t gam[BPT][8];   // gamma as packed pairs
   if (HAS_GAMMA) {
 #pragma unroll
@@ -327,7 +324,6 @@ __global__ void __launch_bounds__(256) rmsnorm_cta_kernel(
       }
     }
   };
-  float am = 0.0f;  // MODE 1: running |normalised| max of this thread
   uint4 cur[BPT][2], nxt[BPT][2];
   int64_t r = blockIdx.x;
   load_row(r, cur);
@@ -384,10 +380,6 @@ __global__ void __launch_bounds__(256) rmsnorm_cta_kernel(
         if (HAS_GAMMA) f[b][j] = f2mul(f[b][j], gam[b][j]);
       }
       const float amax = in ? fmax_abs16_pairs(f[b]) : 0.0f;
-      if (MODE == 1) {
-        am = fmaxf(am, amax);
-        continue;
-      }
       const uint32_t code = in ? block_code(amax, inv_g) : 0u;
       const uint2 packed = encode16_pairs(f[b], inv_tab[code], amax);
       if (in) {
@@ -411,7 +403,102 @@ __global__ void __launch_bounds__(256) rmsnorm_cta_kernel(
       cur[b][1] = nxt[b][1];
     }
   }
-  if (MODE == 1) amax_commit(__float_as_uint(am), ws, g_out, nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// row statistics of the global-scale RMSNorm path (no reference counterpart)
+// ---------------------------------------------------------------------------
+// inv_rms[r] and the amax of (x * inv_rms) * gamma over the whole tensor.  The
+// path has no reference counterpart, so the sum of squares is free of the
+// reference's reduction order: each thread accumulates its 16-element blocks
+// (t, t + 256, ...) in a packed pair of fp32 sums with fma.f32x2, warps reduce
+// with butterflies, and every thread adds the 8 warp sums in the same fixed
+// order, so all threads hold the same 1/RMS after one CTA barrier per row
+// (partials double-buffered across rows).  Persistent CTAs keep the next row
+// in flight.  1/RMS agrees with the reference-order kernel to ~1 ulp.
+template <int BPT, bool HAS_GAMMA>
+__global__ void __launch_bounds__(256) rms_stats_kernel(const uint16_t* __restrict__ x,
+                                                        const uint16_t* __restrict__ gamma,
+                                                        float* __restrict__ inv_rms_out, int64_t rows, int64_t k,
+                                                        float eps, uint32_t* ws, float* g_out) {
+  __shared__ float red[2][8];
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  const int64_t nblk = k >> 4;
+  uint64_t gam[BPT][8];
+  if (HAS_GAMMA) {
+#pragma unroll
+    for (int b = 0; b < BPT; ++b) {
+      const int64_t c = t + 256 * b;
+      uint4 g0 = make_uint4(0, 0, 0, 0), g1 = g0;
+      if (c < nblk) {
+        const uint4* gp = reinterpret_cast<const uint4*>(gamma + 16 * c);
+        g0 = __ldg(gp);
+        g1 = __ldg(gp + 1);
+      }
+      const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) gam[b][j] = bf16x2_to_f2(gw[j]);
+    }
+  }
+  auto load_row = [&](int64_t r, uint4 (&buf)[BPT][2]) {
+#pragma unroll
+    for (int b = 0; b < BPT; ++b) {
+      const int64_t c = t + 256 * b;
+      buf[b][0] = make_uint4(0, 0, 0, 0);
+      buf[b][1] = buf[b][0];
+      if (r < rows && c < nblk) {
+        const uint4* p = reinterpret_cast<const uint4*>(x + r * k + 16 * c);
+        buf[b][0] = __ldg(p);
+        buf[b][1] = __ldg(p + 1);
+      }
+    }
+  };
+  const float inv_k = 1.0f / (float)k;
+  float am = 0.0f;
+  uint4 cur[BPT][2], nxt[BPT][2];
+  int64_t r = blockIdx.x;
+  load_row(r, cur);
+  for (int it = 0; r < rows; r += gridDim.x, ++it) {
+    load_row(r + gridDim.x, nxt);
+    uint64_t f[BPT][8];
+    uint64_t acc = 0;   // packed (0.0f, 0.0f)
+#pragma unroll
+    for (int b = 0; b < BPT; ++b) {
+      const uint32_t w[8] = {cur[b][0].x, cur[b][0].y, cur[b][0].z, cur[b][0].w,
+                             cur[b][1].x, cur[b][1].y, cur[b][1].z, cur[b][1].w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        f[b][j] = bf16x2_to_f2(w[j]);
+        acc = f2fma(f[b][j], f[b][j], acc);   // out-of-range blocks were loaded as zeros
+      }
+    }
+    float ss = f2lo(acc) + f2hi(acc);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (lane == 0) red[it & 1][wid] = ss;
+    __syncthreads();
+    const float* rw = red[it & 1];
+    const float tot = ((rw[0] + rw[1]) + (rw[2] + rw[3])) + ((rw[4] + rw[5]) + (rw[6] + rw[7]));
+    const float inv = rsqrtf(tot * inv_k + eps);
+    if (t == 0) inv_rms_out[r] = inv;
+    const uint64_t inv2 = f2pack(inv, inv);
+#pragma unroll
+    for (int b = 0; b < BPT; ++b) {
+      if (t + 256 * b >= nblk) continue;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint64_t y = f2mul(f[b][j], inv2);
+        if (HAS_GAMMA) y = f2mul(y, gam[b][j]);
+        am = fmaxf(am, fmaxf(fabsf(f2lo(y)), fabsf(f2hi(y))));
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < BPT; ++b) {
+      cur[b][0] = nxt[b][0];
+      cur[b][1] = nxt[b][1];
+    }
+  }
+  amax_commit(__float_as_uint(am), ws, g_out, nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -655,12 +742,11 @@ static int check_quant_args(const void* x, const void* q, const void* s, int64_t
   return NVFP4B200_OK;
 }
 
-template <int MODE>
 static int launch_rms_cta(const void* x, const void* gamma, void* q, void* s, float* inv_rms, int64_t rows, int64_t k,
-                          float eps, const float* g, uint32_t* ws, float* g_out, cudaStream_t st) {
+                          float eps, const float* g, cudaStream_t st) {
   const int64_t pad_rows = round_up(rows, 128), pad_cols = round_up(k / 16, 4);
-  const int64_t cover = MODE == 0 ? pad_rows : rows;
-  const int64_t span = MODE == 0 ? pad_cols : k / 16;  // blocks a CTA must cover
+  const int64_t cover = pad_rows;
+  const int64_t span = pad_cols;  // blocks a CTA must cover
   const int bpt = (int)ceil_div(span, 256);
   const int threads = (int)std::min<int64_t>(256, round_up(span, 32));
   const int q8 = (q == nullptr || aligned(q, 8)) ? 1 : 0;
@@ -673,12 +759,12 @@ static int launch_rms_cta(const void* x, const void* gamma, void* q, void* s, fl
     const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(cover, (int64_t)sms * per_sm));
     kern<<<(unsigned)grid, threads, 0, st>>>(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gamma),
                                              static_cast<uint8_t*>(q), static_cast<uint8_t*>(s), inv_rms, rows,
-                                             pad_rows, k, pad_cols, eps, g, ws, g_out, q8);
+                                             pad_rows, k, pad_cols, eps, g, q8);
     return launch_status();
   };
 #define NVFP4_RMS_CASE(B)                                                         \
   if (bpt <= B)                                                                   \
-    return gamma ? run(rmsnorm_cta_kernel<B, true, MODE>) : run(rmsnorm_cta_kernel<B, false, MODE>);
+    return gamma ? run(rmsnorm_cta_kernel<B, true>) : run(rmsnorm_cta_kernel<B, false>);
   NVFP4_RMS_CASE(1)
   NVFP4_RMS_CASE(2)
   NVFP4_RMS_CASE(4)
@@ -750,7 +836,7 @@ int nvfp4b200_rmsnorm_quant_nvfp4(const void* x, const void* gamma, void* q, voi
   if (rows == 0) return NVFP4B200_OK;
   cudaStream_t st = (cudaStream_t)stream;
   if (rms_cta_fits(k))
-    return launch_rms_cta<0>(x, gamma, q, s, inv_rms, rows, k, eps, global_scale, nullptr, nullptr, st);
+    return launch_rms_cta(x, gamma, q, s, inv_rms, rows, k, eps, global_scale, st);
   // wide rows: 1/RMS pass, then the scaled tile quantizer reads x again
   rms_inv_stream_kernel<<<(unsigned)ceil_div(rows, RMS_WARPS), RMS_WARPS * 32, 0, st>>>(
       static_cast<const uint16_t*>(x), inv_rms, rows, k, eps);
@@ -766,8 +852,25 @@ int nvfp4b200_rmsnorm_stats(const void* x, const void* gamma, float* inv_rms, in
   if (!aligned(x, 16) || (gamma && !aligned(gamma, 16)) || !aligned(ws, 4)) return NVFP4B200_ERR_MISALIGNED;
   int rc = check_device();
   if (rc) return rc;
-  return launch_rms_cta<1>(x, gamma, nullptr, nullptr, inv_rms, rows, k, eps, nullptr, ws, global_scale_out,
-                           (cudaStream_t)stream);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const unsigned grid = (unsigned)std::min<int64_t>(rows, (int64_t)sms * 4);
+  cudaStream_t st = (cudaStream_t)stream;
+  auto X = static_cast<const uint16_t*>(x);
+  auto G = static_cast<const uint16_t*>(gamma);
+  const int bpt = (int)ceil_div(k / 16, (int64_t)256);
+  if (bpt == 1) {
+    if (gamma) rms_stats_kernel<1, true><<<grid, 256, 0, st>>>(X, G, inv_rms, rows, k, eps, ws, global_scale_out);
+    else rms_stats_kernel<1, false><<<grid, 256, 0, st>>>(X, G, inv_rms, rows, k, eps, ws, global_scale_out);
+  } else if (bpt == 2) {
+    if (gamma) rms_stats_kernel<2, true><<<grid, 256, 0, st>>>(X, G, inv_rms, rows, k, eps, ws, global_scale_out);
+    else rms_stats_kernel<2, false><<<grid, 256, 0, st>>>(X, G, inv_rms, rows, k, eps, ws, global_scale_out);
+  } else {   // k <= 16384 (rms_cta_fits)
+    if (gamma) rms_stats_kernel<4, true><<<grid, 256, 0, st>>>(X, G, inv_rms, rows, k, eps, ws, global_scale_out);
+    else rms_stats_kernel<4, false><<<grid, 256, 0, st>>>(X, G, inv_rms, rows, k, eps, ws, global_scale_out);
+  }
+  return launch_status();
 }
 
 int nvfp4b200_quant_nvfp4_t(const void* x, const float* row_scale, const void* gamma, void* q, void* s,
