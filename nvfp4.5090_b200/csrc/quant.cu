@@ -414,28 +414,39 @@ __global__ void __launch_bounds__(256) rmsnorm_cta_kernel(
 // (t, t + 256, ...) in a packed pair of fp32 sums with fma.f32x2, warps reduce
 // with butterflies, and every thread adds the 8 warp sums in the same fixed
 // order, so all threads hold the same 1/RMS after one CTA barrier per row
-// (partials double-buffered across rows).  Persistent CTAs keep the next row
-// in flight.  1/RMS agrees with the reference-order kernel to ~1 ulp.
-template <int BPT, bool HAS_GAMMA>
-__global__ void __launch_bounds__(256) rms_stats_kernel(const uint16_t* __restrict__ x,
-                                                        const uint16_t* __restrict__ gamma,
-                                                        float* __restrict__ inv_rms_out, int64_t rows, int64_t k,
-                                                        float eps, uint32_t* ws, float* g_out) {
+// (partials double-buffered across rows).  1/RMS agrees with the
+// reference-order kernel to ~1 ulp.  Persistent CTAs (as many as fit) keep
+// DEPTH rows in flight ahead of the one being reduced and re-read gamma from
+// L1 where that frees registers: with one 32-byte slice per thread (k <= 4096)
+// two rows ahead at 4 CTAs per SM measured 66 us vs 90 us for one row ahead at
+// 32768 x 4096; wider rows already keep 64+ bytes per thread in flight and stay
+// at one row ahead (16384 x 8192: 67.6 us either way).
+template <int BPT, bool HAS_GAMMA, int DEPTH, bool GAMMA_L1>
+__global__ void __launch_bounds__(256, BPT == 1 ? 4 : 1) rms_stats_kernel(const uint16_t* __restrict__ x,
+                                                                        const uint16_t* __restrict__ gamma,
+                                                                        float* __restrict__ inv_rms_out, int64_t rows,
+                                                                        int64_t k, float eps, uint32_t* ws,
+                                                                        float* g_out) {
   __shared__ float red[2][8];
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
   const int64_t nblk = k >> 4;
-  uint64_t gam[BPT][8];
-  if (HAS_GAMMA) {
+  uint64_t gam[GAMMA_L1 ? 1 : BPT][8];
+  auto load_gamma = [&](int b, uint32_t (&gw)[8]) {
+    const int64_t c = t + 256 * b;
+    uint4 g0 = make_uint4(0, 0, 0, 0), g1 = g0;
+    if (c < nblk) {
+      const uint4* gp = reinterpret_cast<const uint4*>(gamma + 16 * c);
+      g0 = __ldg(gp);
+      g1 = __ldg(gp + 1);
+    }
+    gw[0] = g0.x; gw[1] = g0.y; gw[2] = g0.z; gw[3] = g0.w;
+    gw[4] = g1.x; gw[5] = g1.y; gw[6] = g1.z; gw[7] = g1.w;
+  };
+  if (HAS_GAMMA && !GAMMA_L1) {
 #pragma unroll
     for (int b = 0; b < BPT; ++b) {
-      const int64_t c = t + 256 * b;
-      uint4 g0 = make_uint4(0, 0, 0, 0), g1 = g0;
-      if (c < nblk) {
-        const uint4* gp = reinterpret_cast<const uint4*>(gamma + 16 * c);
-        g0 = __ldg(gp);
-        g1 = __ldg(gp + 1);
-      }
-      const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      uint32_t gw[8];
+      load_gamma(b, gw);
 #pragma unroll
       for (int j = 0; j < 8; ++j) gam[b][j] = bf16x2_to_f2(gw[j]);
     }
@@ -454,22 +465,23 @@ __global__ void __launch_bounds__(256) rms_stats_kernel(const uint16_t* __restri
     }
   };
   const float inv_k = 1.0f / (float)k;
+  const int64_t G = gridDim.x;
   float am = 0.0f;
-  uint4 cur[BPT][2], nxt[BPT][2];
+  uint4 buf[DEPTH + 1][BPT][2];   // buf[0]: the row being reduced; buf[1..DEPTH]: rows in flight
   int64_t r = blockIdx.x;
-  load_row(r, cur);
-  for (int it = 0; r < rows; r += gridDim.x, ++it) {
-    load_row(r + gridDim.x, nxt);
-    uint64_t f[BPT][8];
+#pragma unroll
+  for (int d = 0; d < DEPTH; ++d) load_row(r + d * G, buf[d]);
+  for (int it = 0; r < rows; r += G, ++it) {
+    load_row(r + DEPTH * G, buf[DEPTH]);
     uint64_t acc = 0;   // packed (0.0f, 0.0f)
 #pragma unroll
     for (int b = 0; b < BPT; ++b) {
-      const uint32_t w[8] = {cur[b][0].x, cur[b][0].y, cur[b][0].z, cur[b][0].w,
-                             cur[b][1].x, cur[b][1].y, cur[b][1].z, cur[b][1].w};
+      const uint32_t w[8] = {buf[0][b][0].x, buf[0][b][0].y, buf[0][b][0].z, buf[0][b][0].w,
+                             buf[0][b][1].x, buf[0][b][1].y, buf[0][b][1].z, buf[0][b][1].w};
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        f[b][j] = bf16x2_to_f2(w[j]);
-        acc = f2fma(f[b][j], f[b][j], acc);   // out-of-range blocks were loaded as zeros
+        const uint64_t f = bf16x2_to_f2(w[j]);
+        acc = f2fma(f, f, acc);   // out-of-range blocks were loaded as zeros
       }
     }
     float ss = f2lo(acc) + f2hi(acc);
@@ -485,17 +497,24 @@ __global__ void __launch_bounds__(256) rms_stats_kernel(const uint16_t* __restri
 #pragma unroll
     for (int b = 0; b < BPT; ++b) {
       if (t + 256 * b >= nblk) continue;
+      const uint32_t w[8] = {buf[0][b][0].x, buf[0][b][0].y, buf[0][b][0].z, buf[0][b][0].w,
+                             buf[0][b][1].x, buf[0][b][1].y, buf[0][b][1].z, buf[0][b][1].w};
+      uint32_t gw[8];
+      if (HAS_GAMMA && GAMMA_L1) load_gamma(b, gw);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        uint64_t y = f2mul(f[b][j], inv2);
-        if (HAS_GAMMA) y = f2mul(y, gam[b][j]);
+        uint64_t y = f2mul(bf16x2_to_f2(w[j]), inv2);
+        if (HAS_GAMMA) y = f2mul(y, GAMMA_L1 ? bf16x2_to_f2(gw[j]) : gam[b][j]);
         am = fmaxf(am, fmaxf(fabsf(f2lo(y)), fabsf(f2hi(y))));
       }
     }
 #pragma unroll
-    for (int b = 0; b < BPT; ++b) {
-      cur[b][0] = nxt[b][0];
-      cur[b][1] = nxt[b][1];
+    for (int d = 0; d < DEPTH; ++d) {
+#pragma unroll
+      for (int b = 0; b < BPT; ++b) {
+        buf[d][b][0] = buf[d + 1][b][0];
+        buf[d][b][1] = buf[d + 1][b][1];
+      }
     }
   }
   amax_commit(__float_as_uint(am), ws, g_out, nullptr);
@@ -852,25 +871,24 @@ int nvfp4b200_rmsnorm_stats(const void* x, const void* gamma, float* inv_rms, in
   if (!aligned(x, 16) || (gamma && !aligned(gamma, 16)) || !aligned(ws, 4)) return NVFP4B200_ERR_MISALIGNED;
   int rc = check_device();
   if (rc) return rc;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const unsigned grid = (unsigned)std::min<int64_t>(rows, (int64_t)sms * 4);
   cudaStream_t st = (cudaStream_t)stream;
   auto X = static_cast<const uint16_t*>(x);
   auto G = static_cast<const uint16_t*>(gamma);
+  auto run = [&](auto kern) -> int {
+    int per_sm = 0, dev = 0, sms = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0) != cudaSuccess || per_sm < 1)
+      return NVFP4B200_ERR_CUDA;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const unsigned grid = (unsigned)std::min<int64_t>(rows, (int64_t)sms * per_sm);
+    kern<<<grid, 256, 0, st>>>(X, G, inv_rms, rows, k, eps, ws, global_scale_out);
+    return launch_status();
+  };
   const int bpt = (int)ceil_div(k / 16, (int64_t)256);
-  if (bpt == 1) {
-    if (gamma) rms_stats_kernel<1, true><<<grid, 256, 0, st>>>(X, G, inv_rms, rows, k, eps, ws, global_scale_out);
-    else rms_stats_kernel<1, false><<<grid, 256, 0, st>>>(X, G, inv_rms, rows, k, eps, ws, global_scale_out);
-  } else if (bpt == 2) {
-    if (gamma) rms_stats_kernel<2, true><<<grid, 256, 0, st>>>(X, G, inv_rms, rows, k, eps, ws, global_scale_out);
-    else rms_stats_kernel<2, false><<<grid, 256, 0, st>>>(X, G, inv_rms, rows, k, eps, ws, global_scale_out);
-  } else {   // k <= 16384 (rms_cta_fits)
-    if (gamma) rms_stats_kernel<4, true><<<grid, 256, 0, st>>>(X, G, inv_rms, rows, k, eps, ws, global_scale_out);
-    else rms_stats_kernel<4, false><<<grid, 256, 0, st>>>(X, G, inv_rms, rows, k, eps, ws, global_scale_out);
-  }
-  return launch_status();
+  if (bpt == 1) return gamma ? run(rms_stats_kernel<1, true, 2, true>) : run(rms_stats_kernel<1, false, 2, true>);
+  if (bpt == 2) return gamma ? run(rms_stats_kernel<2, true, 1, true>) : run(rms_stats_kernel<2, false, 1, true>);
+  // k <= 16384 (rms_cta_fits)
+  return gamma ? run(rms_stats_kernel<4, true, 1, true>) : run(rms_stats_kernel<4, false, 1, true>);
 }
 
 int nvfp4b200_quant_nvfp4_t(const void* x, const float* row_scale, const void* gamma, void* q, void* s,

@@ -92,15 +92,26 @@ def test_rmsnorm_matches_reference_golden(pkg):
         assert np.array_equal(u8(q), gold[f"{name}__q"]) and np.array_equal(u8(s), gold[f"{name}__s"]), name
 
 
-def test_rmsnorm_stats_and_global_scale_path(pkg):
-    x = (torch.randn(96, 1024, device="cuda") * 4).to(torch.bfloat16)
-    gamma = (1 + 0.1 * torch.randn(1024, device="cuda")).to(torch.bfloat16)
+@pytest.mark.parametrize("rows,k,with_gamma", [(96, 1024, True), (1203, 4096, True), (700, 4000, False),
+                                                (301, 8192, True), (64, 12288, False), (37, 16384, True)])
+def test_rmsnorm_stats_and_global_scale_path(pkg, rows, k, with_gamma):
+    """rmsnorm_stats for one, two and four 16-element slices per thread (k up
+    to 16384, ragged k and row counts that leave CTAs with different row
+    counts): 1/RMS within 2e-6 of float64, the global scale exactly that of
+    (x * inv_rms) * gamma, and the quantizer bit-exact given both."""
+    gen = torch.Generator(device="cuda").manual_seed(rows + k)
+    x = (torch.randn(rows, k, device="cuda", generator=gen) * 4).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(k, device="cuda", generator=gen)).to(torch.bfloat16) if with_gamma else None
     inv, g = pkg.ops.rmsnorm_stats(x, 1e-6, gamma=gamma)
-    xf = orc.bf16_bits_to_f32(bits(x))
-    y = (xf * inv.cpu().numpy()[:, None]).astype(np.float32) * orc.bf16_bits_to_f32(bits(gamma))[None, :]
+    inv_np = inv.cpu().numpy()
+    inv64 = orc.rms_inv(bits(x), 1e-6)
+    assert np.all(np.abs(inv_np - inv64) <= 2e-6 * inv64)
+    y = (orc.bf16_bits_to_f32(bits(x)) * inv_np[:, None]).astype(np.float32)
+    if with_gamma:
+        y = y * orc.bf16_bits_to_f32(bits(gamma))[None, :]
     assert g.item() == float(orc.global_scale_of(y.astype(np.float32)))
     q, s = pkg.ops.quantize(x, global_scale=g, row_scale=inv, gamma=gamma)
-    oq, os_ = orc.rmsnorm_quant_nvfp4(bits(x), inv.cpu().numpy(), bits(gamma), global_scale=g.item())
+    oq, os_ = orc.rmsnorm_quant_nvfp4(bits(x), inv_np, None if gamma is None else bits(gamma), global_scale=g.item())
     assert np.array_equal(u8(q), oq) and np.array_equal(u8(s), os_)
 
 
