@@ -436,9 +436,13 @@ def bench_quant(pkg, args, peaks):
     plain = timeit(lambda: pkg.ops.quantize(x))
     trans = timeit(lambda: pkg.ops.quantize_t(x, global_scale=gs, row_scale=inv, gamma=gamma))
     gb = lambda nbytes, ms: nbytes / (ms * 1e-3) / 1e9
+    # the global scale must be known before any block is encoded, so this path reads x twice:
+    # its own HBM bound is hbm * alg / (alg + R*K*2)
+    two_pass = hbm * alg / (alg + r * k * 2)
     out["rmsnorm_quant_global_scale"] = {
         "gbps": gb(alg, st + qt), "ms": st + qt, "stats_ms": st, "quant_ms": qt,
         "quant_kernel_gbps": gb(alg, qt), "frac_hbm": gb(alg, st + qt) / hbm,
+        "two_pass_bound_gbps": two_pass, "frac_of_two_pass_bound": gb(alg, st + qt) / two_pass,
         "note": "algorithmic bytes R*K*2 + R*K/2 + scales + gamma + inv_rms; stats pass (inv_rms + amax) reads x once more"}
     out["rmsnorm_quant_single_pass"] = {"gbps": gb(alg, fused), "ms": fused, "frac_hbm": gb(alg, fused) / hbm,
                                         "roofline": {"bound": "hbm", "achieved": gb(alg, fused), "peak": hbm,
