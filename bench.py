@@ -603,10 +603,14 @@ def step_breakdown(trainer, x, dy, n_blocks, d, f, micro):
     NVFP4 GEMM launch attributed to its role by its place in the step's fixed
     launch order (per micro-batch: gate/up and down per block forward, then dh,
     dW_down, dxn and dW_gu per block backward).  With a process group the
-    NCCL kernels are separated out: ``exposed_comm_ms`` is the step's span
-    minus the union of its compute-kernel intervals (time in which only
-    collectives run, or nothing)."""
-    import collections
+    NCCL kernels are separated out.  The profiled step ends with ``finish()``,
+    which waits for the parameter all-gathers of the next step; in a stream of
+    steps those overlap the next forward, except the first bucket's, which
+    block 0 waits for.  So: ``exposed_in_step_ms`` is the time between the
+    first and the last compute kernel in which no compute kernel runs,
+    ``trailing_nccl_ms`` the collectives after the last compute kernel, and
+    ``exposed_comm_ms`` = exposed_in_step_ms + the first of those gathers
+    (the steady-state exposure per step)."""
     import torch
     from torch.profiler import ProfilerActivity, profile
     torch.cuda.synchronize()
@@ -616,6 +620,13 @@ def step_breakdown(trainer, x, dy, n_blocks, d, f, micro):
         torch.cuda.synchronize()
     ks = sorted((e.time_range.start, e.time_range.end, e.name) for e in prof.events()
                 if e.device_type == torch.autograd.DeviceType.CUDA)
+    return summarize_kernels(ks, n_blocks, d, f, micro)
+
+
+def summarize_kernels(ks, n_blocks, d, f, micro):
+    """step_breakdown's summary of one step's kernel records ``ks`` = sorted
+    (start_us, end_us, name) tuples."""
+    import collections
     if not ks:
         return {"error": "no kernel records"}
     agg = collections.defaultdict(lambda: [0, 0.0])
@@ -652,6 +663,12 @@ def step_breakdown(trainer, x, dy, n_blocks, d, f, micro):
     if cur is not None:
         union += cur[1] - cur[0]
     nccl_ms = sum((b - a) / 1e3 for a, b, n in ks if "nccl" in n.lower())
+    c_first = comp[0][0] if comp else ks[0][0]
+    c_last = max(b for a, b in comp) if comp else ks[-1][1]
+    in_step = (c_last - c_first) / 1e3 - union / 1e3
+    trailing = sorted((a, b, n) for a, b, n in ks if "nccl" in n.lower() and a >= c_last)
+    trailing_ms = sum((b - a) / 1e3 for a, b, n in trailing)
+    first_gather = next(((b - a) / 1e3 for a, b, n in trailing if "allgather" in n.lower()), 0.0)
     # the largest gaps between compute kernels: where the step waits, and for what
     t0 = ks[0][0]
     comp_named = sorted((a, b, n) for a, b, n in ks if "nccl" not in n.lower())
@@ -666,7 +683,9 @@ def step_breakdown(trainer, x, dy, n_blocks, d, f, micro):
     gaps.sort(key=lambda g: -g["ms"])
     return {
         "span_ms": span, "kernel_busy_ms": busy, "launches": len(ks), "compute_busy_ms": union / 1e3,
-        "nccl_kernel_ms": nccl_ms, "exposed_comm_ms": span - union / 1e3, "largest_gaps": gaps[:8],
+        "nccl_kernel_ms": nccl_ms, "exposed_in_step_ms": in_step, "trailing_nccl_ms": trailing_ms,
+        "first_trailing_gather_ms": first_gather, "exposed_comm_ms": in_step + first_gather,
+        "span_minus_compute_ms": span - union / 1e3, "largest_gaps": gaps[:8],
         "kernels": [{"name": k, "launches": c, "ms": round(ms, 3), "share": round(ms / busy, 4)}
                     for k, (c, ms) in sorted(agg.items(), key=lambda kv: -kv[1][1])[:16]],
         "gemm_roles": {r: {"launches": len(v), "mean_ms": round(sum(v) / len(v), 4),

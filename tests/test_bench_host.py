@@ -44,3 +44,26 @@ def test_reference_arm_other_ranks_exit_without_work(monkeypatch, capsys):
     monkeypatch.setattr(bench, "cpu_gemm_sample", lambda: (_ for _ in ()).throw(AssertionError("ran work")))
     assert bench.main(["--impl", "reference", "--steps", "1", "--warmup", "3"]) == 0
     assert capsys.readouterr().out == ""
+
+
+def test_kernel_summary_exposed_comm():
+    """summarize_kernels on a synthetic step: compute kernels with one gap
+    covered by a reduce-scatter, then the next step's two all-gathers after
+    the last compute kernel.  Steady-state exposure = the in-step gap + the
+    first trailing gather; the trailing gathers are reported apart."""
+    ks = sorted([
+        (0.0, 1000.0, "nvfp4b200::gemm::nvfp4_gemm_kernel(...)"),
+        (1000.0, 1500.0, "quant_tile_kernel"),
+        (1400.0, 2600.0, "ncclDevKernel_ReduceScatter_Sum_bf16_RING_LL"),
+        (2000.0, 3000.0, "nvfp4b200::gemm::nvfp4_gemm_kernel(...)"),   # gap 1500..2000 under the RS
+        (3000.0, 3400.0, "ncclDevKernel_AllGather_RING_LL"),
+        (3400.0, 3900.0, "ncclDevKernel_AllGather_RING_LL"),
+    ])
+    r = bench.summarize_kernels(ks, n_blocks=1, d=64, f=128, micro=16)
+    assert abs(r["compute_busy_ms"] - 2.5) < 1e-9
+    assert abs(r["exposed_in_step_ms"] - 0.5) < 1e-9
+    assert abs(r["trailing_nccl_ms"] - 0.9) < 1e-9
+    assert abs(r["first_trailing_gather_ms"] - 0.4) < 1e-9
+    assert abs(r["exposed_comm_ms"] - 0.9) < 1e-9
+    assert abs(r["span_minus_compute_ms"] - 1.4) < 1e-9
+    assert r["largest_gaps"][0]["ms"] == 0.5 and r["largest_gaps"][0]["nccl_running"] == ["ncclDevKernel_ReduceScatter_Sum_bf16_RING_LL"]
