@@ -465,7 +465,8 @@ def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=No
     t_local = global_tokens // world
     trainer = NVFP4MLPStackTrainer(n_blocks, d, f, device="cuda", seed=seed, micro_tokens=micro_tokens,
                                    process_group=pg, max_local_tokens=t_local,
-                                   comm_sms=getattr(args, "comm_sms", 0), zero=not getattr(args, "allreduce", False))
+                                   comm_sms=getattr(args, "comm_sms", 0), zero=not getattr(args, "allreduce", False),
+                                   shard_quant=False if getattr(args, "bf16_gather", False) else None)
     g = torch.Generator(device="cuda").manual_seed(seed * 1000 + rank)
     x = torch.randn(t_local, d, device="cuda", generator=g).to(torch.bfloat16)
     dy = (torch.randn(t_local, d, device="cuda", generator=g) * 1e-3).to(torch.bfloat16)
@@ -489,8 +490,13 @@ def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=No
            "flops_per_step": flops, "n_gpus": world, "tokens_global": global_tokens, "tokens_per_rank": t_local,
            "micro_tokens": micro_tokens, "clocks": clk.summary(), "finite": bool(torch.isfinite(r).all().item())}
     if world > 1:
-        res["exchange"] = ("ZeRO-1: reduce-scatter + sharded AdamW + all-gather" if trainer.opt is not None
-                           else "all-reduce + replicated AdamW")
+        if trainer.layout is not None:
+            res["exchange"] = ("ZeRO-1: reduce-scatter + sharded AdamW, each rank quantizes its rows of the "
+                               "updated weights, all-gather of NVFP4 weights")
+        elif trainer.opt is not None:
+            res["exchange"] = "ZeRO-1: reduce-scatter + sharded AdamW + all-gather of bf16 parameters"
+        else:
+            res["exchange"] = "all-reduce + replicated AdamW"
         res["comm_sms"] = trainer.comm_sms
     # e2e through the public API: pinned host tokens + upstream grad copied in, step result read back
     hx = x.cpu().pin_memory()
@@ -885,6 +891,9 @@ def main(argv=None):
                     help="MLP stack at N > 1: SMs left free of GEMMs for the NCCL kernels (0 = none)")
     ap.add_argument("--allreduce", action="store_true",
                     help="MLP stack at N > 1: plain all-reduce + replicated AdamW instead of ZeRO-1")
+    ap.add_argument("--bf16-gather", action="store_true",
+                    help="MLP stack at N > 1 (ZeRO-1): gather bf16 parameters and quantize all weights on every "
+                         "rank instead of gathering each rank's quantized rows")
     ap.add_argument("--breakdown", action="store_true",
                     help="after the timed MLP steps, one more step under torch.profiler: per-kernel device time")
     ap.add_argument("--only", choices=["gemm", "gemm_sweep", "quant", "mlp_block", "mlp_stack"], default=None,
@@ -980,8 +989,9 @@ def main(argv=None):
         line["mlp_stack"] = bench_mlp(pkg, args, world, rank, 8, 8192, 28672, 65536, seed=4, pg=pg)
         line["mlp_stack"]["workload"] = ("8 RMSNorm+SwiGLU blocks, d=8192, ff=28672, 65536 global tokens split "
                                          "across ranks; at N > 1 ZeRO-1: bf16 wgrad reduce-scatter (NCCL) overlapped "
-                                         "with backward, AdamW on each rank's 1/N shard, bf16 parameter all-gather "
-                                         "overlapped with the next step's forward")
+                                         "with backward, AdamW on each rank's 1/N shard, each rank quantizes its "
+                                         "rows of the updated weights, NVFP4 weight all-gather overlapped with the "
+                                         "next step's forward")
         line["mlp_stack"]["scaling"] = "strong"
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -77,16 +77,29 @@ def workspace(device: torch.device) -> torch.Tensor:
 # ----------------------------------------------------------------------------
 
 
+def _outputs(out, q_shape, s_shape, device):
+    """(q, s) to write: new tensors, or the caller's ``out`` pair checked for
+    shape, dtype, device and contiguity (e.g. slots of a gather buffer)."""
+    if out is None:
+        return (torch.empty(q_shape, device=device, dtype=torch.uint8),
+                torch.empty(s_shape, device=device, dtype=torch.uint8))
+    q, s = out
+    for t, shape, name in ((q, q_shape, "q"), (s, s_shape, "s")):
+        _require(t.dtype == torch.uint8 and tuple(t.shape) == tuple(shape) and t.is_contiguous()
+                 and t.device == device, f"out {name} must be a contiguous uint8 {tuple(shape)} tensor on {device}")
+    return q, s
+
+
 def quantize(x: torch.Tensor, global_scale: Optional[torch.Tensor] = None,
-             row_scale: Optional[torch.Tensor] = None, gamma: Optional[torch.Tensor] = None):
-    """Quantize a bf16 [R, K] matrix along K -> (q u8 [R, K/2], s u8 swizzled)."""
+             row_scale: Optional[torch.Tensor] = None, gamma: Optional[torch.Tensor] = None, out=None):
+    """Quantize a bf16 [R, K] matrix along K -> (q u8 [R, K/2], s u8 swizzled);
+    ``out=(q, s)`` writes into given tensors of those shapes."""
     _check_bf16(x, "quantize")
     _require(x.dim() == 2, "quantize expects a 2-D tensor")
     x = x.contiguous()
     r, k = x.shape
     _require(k % 16 == 0, "K must be divisible by 16 for NVFP4 1x16 scaling.")
-    q = torch.empty((r, k // 2), device=x.device, dtype=torch.uint8)
-    s = torch.empty(scale_shape(r, k), device=x.device, dtype=torch.uint8)
+    q, s = _outputs(out, (r, k // 2), scale_shape(r, k), x.device)
     g = _scalar_f32(global_scale, x.device)
     if row_scale is not None:
         _require(row_scale.dtype == torch.float32 and row_scale.numel() == r, "row_scale is float32 [R]")
@@ -138,14 +151,14 @@ def rmsnorm_stats(x: torch.Tensor, eps: float = 1e-6, gamma: Optional[torch.Tens
 
 
 def quantize_t(x: torch.Tensor, global_scale: Optional[torch.Tensor] = None,
-               row_scale: Optional[torch.Tensor] = None, gamma: Optional[torch.Tensor] = None):
-    """Quantize x^T (x bf16 [R, C]) along R -> (q u8 [C, R/2], s swizzled for (C, R))."""
+               row_scale: Optional[torch.Tensor] = None, gamma: Optional[torch.Tensor] = None, out=None):
+    """Quantize x^T (x bf16 [R, C]) along R -> (q u8 [C, R/2], s swizzled for (C, R));
+    ``out=(q, s)`` writes into given tensors of those shapes."""
     _check_bf16(x, "quantize_t")
     x = x.contiguous()
     r, c = x.shape
     _require(r % 16 == 0 and c % 8 == 0, "quantize_t needs rows % 16 == 0 and cols % 8 == 0")
-    q = torch.empty((c, r // 2), device=x.device, dtype=torch.uint8)
-    s = torch.empty(scale_shape(c, r), device=x.device, dtype=torch.uint8)
+    q, s = _outputs(out, (c, r // 2), scale_shape(c, r), x.device)
     g = _scalar_f32(global_scale, x.device)
     if row_scale is not None:
         row_scale = row_scale.contiguous()

@@ -2,12 +2,15 @@
 
 Two ranks each take half of a 512-token batch; the single-rank trainer runs
 the same batch as two micro-batches of the same 256 tokens, so every global
-scale of every GEMM operand is the same in both runs.  Checks:
+scale of every GEMM operand is the same in both runs.  Three exchanges run:
+ZeRO-1 with sharded weight quantization (rank-major buckets, NVFP4 weights
+gathered), ZeRO-1 gathering bf16 parameters, and all-reduce.  Checks:
 
-* ZeRO-1 (reduce-scatter, sharded AdamW with fp32 masters, all-gather) and
-  the all-reduce path give bit-identical parameters after two steps (a sum of
+* all three give bit-identical fp32 master weights after two steps (a sum of
   two bf16 gradients does not depend on the collective; the AdamW update is
-  element-wise);
+  element-wise) and bit-identical NVFP4 weights for the next step (codes,
+  swizzled scales and global scales of both orientations), whether every
+  rank quantized all weights or only its rows before the gather;
 * the all-reduced gradient bucket equals the single-rank gradient (fp32
   accumulation of the two micro-batches) within two bf16 roundings
   (relative Frobenius error <= 1e-2);
@@ -27,6 +30,8 @@ import torch
 pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 T_LOCAL, D, F, BLOCKS = 256, 256, 512, 2
+MODES = ("zero_sq", "zero_flat", "allreduce")
+QFIELDS = ("g_gu", "g_down", "q_gu", "s_gu", "q_down", "s_down", "q_gu_t", "s_gu_t", "q_down_t", "s_down_t")
 
 
 def _free_port():
@@ -52,7 +57,7 @@ def _mlp():
     return importlib.import_module("nvfp4_b200.mlp")
 
 
-def _worker(rank, world, port, zero, out_path):
+def _worker(rank, world, port, mode, out_path):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -61,34 +66,36 @@ def _worker(rank, world, port, zero, out_path):
                             device_id=torch.device("cuda", rank))
     try:
         mlp = _mlp()
+        ops = sys.modules["nvfp4_b200"].ops
         x, dy = _batch(world)
         lo, hi = rank * T_LOCAL, (rank + 1) * T_LOCAL
+        sq = {"zero_sq": True, "zero_flat": False, "allreduce": None}[mode]
         tr = mlp.NVFP4MLPStackTrainer(BLOCKS, D, F, seed=7, micro_tokens=T_LOCAL, max_local_tokens=T_LOCAL,
-                                      process_group=dist.group.WORLD, zero=zero)
-        p0 = [b.param[:b.numel].clone() for b in tr.blocks]
+                                      process_group=dist.group.WORLD, zero=mode != "allreduce", shard_quant=sq)
+        assert (tr.layout is not None) == (mode == "zero_sq")
+        p0 = [tuple(t.cpu() for t in m) for m in tr.gather_masters()]
         tr.step(x[lo:hi], dy[lo:hi])
-        grads = None if zero else [b.grad[:b.numel].clone() for b in tr.blocks]   # summed over ranks
+        grads = [b.grad[:b.numel].clone() for b in tr.blocks] if mode == "allreduce" else None   # summed over ranks
         tr.step(x[lo:hi], dy[lo:hi])
         tr.finish()
         torch.cuda.synchronize()
-        masters = None
-        if not zero:
-            masters = [b.master[:b.numel].cpu() for b in tr.blocks]
-        else:   # gather the fp32 master shards
-            masters = []
-            for i, b in enumerate(tr.blocks):
-                w = tr.opt.w[i]
-                full = torch.empty(w.numel() * world, device="cuda", dtype=torch.float32)
-                dist.all_gather_into_tensor(full, w)
-                masters.append(full[:b.numel].cpu())
-        # the weight global scales of the next step (shard amaxes, max over ranks) are the weights' own
-        for i, b in enumerate(tr.blocks):
-            assert torch.equal(tr.w_g[i, 0:1], sys.modules["nvfp4_b200"].ops.global_scale(b.w_gu))
-            assert torch.equal(tr.w_g[i, 1:2], sys.modules["nvfp4_b200"].ops.global_scale(b.w_down))
+        masters = [tuple(t.cpu() for t in m) for m in tr.gather_masters()]
+        qws = []
+        for i, b in enumerate(tr.blocks):   # the NVFP4 weights the next step would use
+            if tr.layout is not None:
+                q = tr.gathered[i].qweights(tr.w_g[i, 0:1], tr.w_g[i, 1:2])
+            else:
+                q = mlp.quantize_weights(b.w_gu, b.w_down, g_gu=tr.w_g[i, 0:1], g_down=tr.w_g[i, 1:2])
+            qws.append({k: getattr(q, k).cpu() for k in QFIELDS})
+        # the global scales of the next step (shard amaxes, max over ranks) are the weights' own
+        for i, (_, wgu, wdn) in enumerate(masters):
+            assert torch.equal(tr.w_g[i, 0:1], ops.global_scale(wgu.cuda().to(torch.bfloat16)))
+            assert torch.equal(tr.w_g[i, 1:2], ops.global_scale(wdn.cuda().to(torch.bfloat16)))
+        torch.cuda.synchronize()
         if rank == 0:
-            torch.save({"params": [b.param[:b.numel].cpu() for b in tr.blocks], "p0": [p.cpu() for p in p0],
-                        "grads": None if grads is None else [g.cpu() for g in grads], "masters": masters,
-                        "device_error": sys.modules["nvfp4_b200"].ops.device_error()}, out_path)
+            torch.save({"p0": p0, "masters": masters, "qws": qws,
+                        "grads": None if grads is None else [g.cpu() for g in grads],
+                        "device_error": ops.device_error()}, out_path)
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -99,21 +106,26 @@ def test_two_rank_trainer_matches_single_rank(pkg, tmp_path):
     import torch.multiprocessing as mp
     world = 2
     res = {}
-    for zero in (True, False):
-        path = str(tmp_path / f"zero{int(zero)}.pt")
-        mp.spawn(_worker, args=(world, _free_port(), zero, path), nprocs=world, join=True)
-        res[zero] = torch.load(path)
-        assert res[zero]["device_error"] == 0
-    for a, b in zip(res[True]["params"], res[False]["params"]):
-        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
-    for a, b in zip(res[True]["masters"], res[False]["masters"]):
-        assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+    for mode in MODES:
+        path = str(tmp_path / f"{mode}.pt")
+        mp.spawn(_worker, args=(world, _free_port(), mode, path), nprocs=world, join=True)
+        res[mode] = torch.load(path)
+        assert res[mode]["device_error"] == 0
+    ref = res["allreduce"]
+    for mode in ("zero_sq", "zero_flat"):
+        for a, b in zip(res[mode]["masters"], ref["masters"]):
+            for x, y in zip(a, b):
+                assert torch.equal(x.view(torch.int32), y.view(torch.int32)), mode
+        for qa, qb in zip(res[mode]["qws"], ref["qws"]):
+            for k in QFIELDS:
+                assert torch.equal(qa[k], qb[k]), (mode, k)
 
     mlp = _mlp()
     x, dy = _batch(world)
     single = mlp.NVFP4MLPStackTrainer(BLOCKS, D, F, seed=7, micro_tokens=T_LOCAL, max_local_tokens=world * T_LOCAL)
-    for b, p0 in zip(single.blocks, res[False]["p0"]):
-        assert torch.equal(b.param[:b.numel].cpu().view(torch.int16), p0.view(torch.int16))
+    for b, (gam, wgu, wdn) in zip(single.blocks, ref["p0"]):
+        p = b.param[:b.numel].cpu().float()
+        assert torch.equal(p, torch.cat([gam, wgu.flatten(), wdn.flatten()]))
     single.step(x, dy)
     # one rank with two micro-batches: the gradient is the fp32 accumulators
     g1 = [torch.cat([b.grad_gamma32, b.acc_gu.flatten(), b.acc_down.flatten()]).cpu() for b in single.blocks]
@@ -121,11 +133,11 @@ def test_two_rank_trainer_matches_single_rank(pkg, tmp_path):
     torch.cuda.synchronize()
     assert pkg.ops.device_error() == 0
     rel = lambda a, b: ((a.float() - b.float()).norm() / b.float().norm()).item()
-    for gd, gs in zip(res[False]["grads"], g1):
+    for gd, gs in zip(ref["grads"], g1):
         assert rel(gd, gs) < 1e-2
-    for blk, md, p0 in zip(single.blocks, res[False]["masters"], res[False]["p0"]):
-        ud = md - p0.float()
-        us = blk.master[:blk.numel].cpu() - p0.float()
+    for blk, md, p0 in zip(single.blocks, ref["masters"], ref["p0"]):
+        ud = torch.cat([t.flatten() for t in md]) - torch.cat([t.flatten() for t in p0])
+        us = blk.master[:blk.numel].cpu() - torch.cat([t.flatten() for t in p0])
         cos = torch.nn.functional.cosine_similarity(ud, us, dim=0).item()
         assert cos > 0.99
         agree = (torch.sign(ud) == torch.sign(us)).float().mean().item()
