@@ -523,7 +523,9 @@ def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=No
                   "h2d_bytes_per_step": 2 * x.numel() * 2 * world, "d2h_bytes_per_step": 4 * world,
                   "pipeline": PIPELINE_NOTE}
     if getattr(args, "breakdown", False):   # every rank runs the profiled step (it holds collectives)
-        bd = step_breakdown(trainer, x, dy, n_blocks, d, f, min(micro_tokens, t_local))
+        # rank-major buckets with one micro-batch: each wgrad GEMM is one launch per rank's row block
+        splits = world if (trainer.layout is not None and t_local <= micro_tokens) else 1
+        bd = step_breakdown(trainer, x, dy, n_blocks, d, f, min(micro_tokens, t_local), wgrad_splits=splits)
         if world > 1:
             bd["exposed_comm_ms_max_over_ranks"] = max_over_ranks(bd.get("exposed_comm_ms", 0.0), world)
         res["kernel_breakdown"] = bd
@@ -603,7 +605,7 @@ def pipelined_e2e(steps, upload, compute, download, finish=None):
     return e0.elapsed_time(e1)
 
 
-def step_breakdown(trainer, x, dy, n_blocks, d, f, micro):
+def step_breakdown(trainer, x, dy, n_blocks, d, f, micro, wgrad_splits=1):
     """One extra training step under torch.profiler (CUPTI kernel records, the
     real overlap, outside every timed region): device time per kernel, and each
     NVFP4 GEMM launch attributed to its role by its place in the step's fixed
@@ -626,12 +628,13 @@ def step_breakdown(trainer, x, dy, n_blocks, d, f, micro):
         torch.cuda.synchronize()
     ks = sorted((e.time_range.start, e.time_range.end, e.name) for e in prof.events()
                 if e.device_type == torch.autograd.DeviceType.CUDA)
-    return summarize_kernels(ks, n_blocks, d, f, micro)
+    return summarize_kernels(ks, n_blocks, d, f, micro, wgrad_splits)
 
 
-def summarize_kernels(ks, n_blocks, d, f, micro):
+def summarize_kernels(ks, n_blocks, d, f, micro, wgrad_splits=1):
     """step_breakdown's summary of one step's kernel records ``ks`` = sorted
-    (start_us, end_us, name) tuples."""
+    (start_us, end_us, name) tuples; each wgrad GEMM is ``wgrad_splits``
+    launches (row blocks), whose times are summed per role occurrence."""
     import collections
     if not ks:
         return {"error": "no kernel records"}
@@ -641,18 +644,24 @@ def summarize_kernels(ks, n_blocks, d, f, micro):
         agg[key][0] += 1
         agg[key][1] += (b - a) / 1e3
     gem = [(b - a) / 1e3 for a, b, n in ks if "nvfp4_gemm_kernel" in n]
-    per_micro = 6 * n_blocks
     t = micro
     flop = {"fwd_gate_up_swiglu": 2 * t * 2 * f * d, "fwd_down": 2 * t * d * f, "bwd_dh_swiglu": 2 * t * f * d,
             "wgrad_down": 2 * d * f * t, "bwd_dxn": 2 * t * d * 2 * f, "wgrad_gate_up": 2 * 2 * f * d * t}
+    # the step's fixed GEMM launch order per micro-batch: gate/up and down per
+    # block forward, then dh, dW_down, dxn, dW_gu per block backward
+    sp = max(1, int(wgrad_splits))
+    order = ["fwd_gate_up_swiglu", "fwd_down"] * n_blocks + (
+        ["bwd_dh_swiglu"] + ["wgrad_down"] * sp + ["bwd_dxn"] + ["wgrad_gate_up"] * sp) * n_blocks
     roles = collections.defaultdict(list)
+    prev = None
     for i, ms in enumerate(gem):
-        j = i % per_micro
-        if j < 2 * n_blocks:
-            r = "fwd_gate_up_swiglu" if j % 2 == 0 else "fwd_down"
+        j = i % len(order)
+        r = order[j]
+        if sp > 1 and r.startswith("wgrad") and prev is not None and prev[0] == r and prev[1] == j - 1:
+            roles[r][-1] += ms          # another row block of the same wgrad GEMM
         else:
-            r = ["bwd_dh_swiglu", "wgrad_down", "bwd_dxn", "wgrad_gate_up"][(j - 2 * n_blocks) % 4]
-        roles[r].append(ms)
+            roles[r].append(ms)
+        prev = (r, j)
     busy = sum(v[1] for v in agg.values())
     span = (ks[-1][1] - ks[0][0]) / 1e3
     # collectives: time during which only NCCL kernels (or nothing) run, i.e. the

@@ -67,3 +67,22 @@ def test_kernel_summary_exposed_comm():
     assert abs(r["exposed_comm_ms"] - 0.9) < 1e-9
     assert abs(r["span_minus_compute_ms"] - 1.4) < 1e-9
     assert r["largest_gaps"][0]["ms"] == 0.5 and r["largest_gaps"][0]["nccl_running"] == ["ncclDevKernel_ReduceScatter_Sum_bf16_RING_LL"]
+
+
+def test_kernel_summary_wgrad_splits():
+    """With rank-major buckets each wgrad GEMM is several launches: the role
+    time sums a GEMM's row blocks, and the other roles keep their place."""
+    g = "nvfp4b200::gemm::nvfp4_gemm_kernel"
+    dur = {"fwd_gate_up_swiglu": 300.0, "fwd_down": 200.0, "bwd_dh_swiglu": 250.0, "wgrad_down": 50.0,
+           "bwd_dxn": 400.0, "wgrad_gate_up": 100.0}
+    seq = ["fwd_gate_up_swiglu", "fwd_down"] * 2 + (["bwd_dh_swiglu"] + ["wgrad_down"] * 4 + ["bwd_dxn"]
+                                                    + ["wgrad_gate_up"] * 4) * 2
+    ks, t = [], 0.0
+    for r in seq:
+        ks.append((t, t + dur[r], g))
+        t += dur[r]
+    out = bench.summarize_kernels(ks, n_blocks=2, d=64, f=128, micro=16, wgrad_splits=4)["gemm_roles"]
+    assert out["wgrad_down"]["launches"] == 2 and abs(out["wgrad_down"]["mean_ms"] - 0.2) < 1e-9
+    assert out["wgrad_gate_up"]["launches"] == 2 and abs(out["wgrad_gate_up"]["mean_ms"] - 0.4) < 1e-9
+    assert out["bwd_dxn"]["launches"] == 2 and abs(out["bwd_dxn"]["mean_ms"] - 0.4) < 1e-9
+    assert out["fwd_down"]["launches"] == 2 and abs(out["fwd_down"]["mean_ms"] - 0.2) < 1e-9
