@@ -315,14 +315,14 @@ class GatheredWeights:
         self.ps_gu_t = torch.empty((n,) + ops.scale_shape(d, r1), **u8)
         self.pq_down_t = torch.empty((n, f, r2 // 2), **u8)
         self.ps_down_t = torch.empty((n,) + ops.scale_shape(f, r2), **u8)
-        self.works: List[object] = []
+        self.works: List[object] = []      # gathers of gamma and the row-wise weights (forward)
+        self.works_t: List[object] = []    # gathers of the transposed pieces (backward)
         self.permuted = True
 
-    def quantize_and_gather(self, rank: int, param: torch.Tensor, g_gu: torch.Tensor, g_down: torch.Tensor,
-                            pg) -> None:
-        """Quantize this rank's rows of the block (rank-major param bucket) with the
-        weights' global scales and start the all-gathers of every rank's pieces."""
-        import torch.distributed as dist
+    def quantize(self, rank: int, param: torch.Tensor, g_gu: torch.Tensor, g_down: torch.Tensor) -> None:
+        """Quantize this rank's rows of the block (rank-major param bucket) in
+        both orientations with the weights' global scales, into the slots the
+        gathers send from."""
         lay, r = self.lay, rank
         gu_r, down_r = lay.gu_pieces(param)[r], lay.down_pieces(param)[r]
         a1, b1 = r * lay.r1, (r + 1) * lay.r1
@@ -331,20 +331,51 @@ class GatheredWeights:
         ops.quantize(down_r, global_scale=g_down, out=(self.q_down[a2:b2], self.s_down[a2:b2]))
         ops.quantize_t(gu_r, global_scale=g_gu, out=(self.pq_gu_t[r], self.ps_gu_t[r]))
         ops.quantize_t(down_r, global_scale=g_down, out=(self.pq_down_t[r], self.ps_down_t[r]))
+        self.permuted = False
+
+    def gather_forward(self, rank: int, param: torch.Tensor, pg) -> None:
+        """Start the all-gathers of gamma and the row-wise NVFP4 weights (what the forward uses)."""
+        import torch.distributed as dist
+        lay, r = self.lay, rank
+        a1, b1 = r * lay.r1, (r + 1) * lay.r1
+        a2, b2 = r * lay.r2, (r + 1) * lay.r2
         works = [dist.all_gather_into_tensor(self.gamma, lay.gamma_pieces(param)[r], group=pg, async_op=True)]
         for full, lo, hi in ((self.q_gu, a1, b1), (self.s_gu, a1, b1), (self.q_down, a2, b2), (self.s_down, a2, b2)):
             works.append(dist.all_gather_into_tensor(full.view(-1), full[lo:hi].view(-1), group=pg, async_op=True))
-        for buf in (self.pq_gu_t, self.ps_gu_t, self.pq_down_t, self.ps_down_t):   # in place, rank-major
-            works.append(dist.all_gather_into_tensor(buf.view(-1), buf[r].view(-1), group=pg, async_op=True))
         self.works = works
-        self.permuted = False
+
+    def gather_transposed(self, rank: int, pg) -> None:
+        """Start the all-gathers of the transposed pieces (in place, rank-major; first used by the backward)."""
+        import torch.distributed as dist
+        self.works_t = [dist.all_gather_into_tensor(buf.view(-1), buf[rank].view(-1), group=pg, async_op=True)
+                        for buf in (self.pq_gu_t, self.ps_gu_t, self.pq_down_t, self.ps_down_t)]
+
+    def quantize_and_gather(self, rank: int, param: torch.Tensor, g_gu: torch.Tensor, g_down: torch.Tensor,
+                            pg) -> None:
+        self.quantize(rank, param, g_gu, g_down)
+        self.gather_forward(rank, param, pg)
+        self.gather_transposed(rank, pg)
+
+    def wait(self) -> None:
+        """Make the current stream wait for every gather of the block still in flight."""
+        for w in self.works + self.works_t:
+            w.wait()
+        self.works, self.works_t = [], []
 
     def qweights(self, g_gu: torch.Tensor, g_down: torch.Tensor) -> QWeights:
-        """Wait (on the current stream) for the gathers, put the transposed
-        pieces in place, and return the block's QWeights."""
+        """Wait (on the current stream) for the forward's gathers and return the
+        block's QWeights; the transposed fields are valid after ensure_transposed()."""
         for w in self.works:
             w.wait()
         self.works = []
+        return QWeights(g_gu, g_down, self.q_gu, self.s_gu, self.q_down, self.s_down, self.q_gu_t, self.s_gu_t,
+                        self.q_down_t, self.s_down_t)
+
+    def ensure_transposed(self) -> None:
+        """Wait for the transposed pieces and put them in place (once per gather)."""
+        for w in self.works_t:
+            w.wait()
+        self.works_t = []
         if not self.permuted:
             lay, n = self.lay, self.lay.world
             d, f, r1, r2 = lay.d, lay.f, lay.r1, lay.r2
@@ -358,8 +389,6 @@ class GatheredWeights:
                 full.view(i64).view(groups, n, kr // 64, 64).copy_(
                     pieces.view(i64).view(n, groups, kr // 64, 64).permute(1, 0, 2, 3))
             self.permuted = True
-        return QWeights(g_gu, g_down, self.q_gu, self.s_gu, self.q_down, self.s_down, self.q_gu_t, self.s_gu_t,
-                        self.q_down_t, self.s_down_t)
 
 
 class BlockState:
@@ -543,6 +572,8 @@ class NVFP4MLPStackTrainer:
             last = mi == n_micro - 1
             for bi in reversed(range(self.n_blocks)):
                 b = self.blocks[bi]
+                if lay is not None:
+                    self.gathered[bi].ensure_transposed()
                 if n_micro == 1:
                     # rank-major buckets: one wgrad GEMM per rank's row block
                     tgt_gu = lay.gu_pieces(b.grad) if lay is not None else b.grad_gu
@@ -644,10 +675,14 @@ class NVFP4MLPStackTrainer:
             # gathers in the order the next forward uses the blocks: block 0 lands first
             for bi, b in enumerate(self.blocks):
                 if lay is not None:
-                    self.gathered[bi].quantize_and_gather(self.opt.rank, b.param, self.w_g[bi, 0:1],
-                                                          self.w_g[bi, 1:2], self.pg)
+                    gw = self.gathered[bi]
+                    gw.quantize(self.opt.rank, b.param, self.w_g[bi, 0:1], self.w_g[bi, 1:2])
+                    gw.gather_forward(self.opt.rank, b.param, self.pg)
                 else:
                     self.opt.gather(bi, b.param)
+            if lay is not None:   # the backward needs the last block's transposed weights first
+                for bi in reversed(range(self.n_blocks)):
+                    self.gathered[bi].gather_transposed(self.opt.rank, self.pg)
         return out_sum
 
     def _shard_amax(self) -> None:
@@ -667,8 +702,11 @@ class NVFP4MLPStackTrainer:
         dist.all_reduce(self.w_amax, op=dist.ReduceOp.MAX, group=self.pg)
         self.w_g = ops.global_scale_from_amax(self.w_amax)
         for bi, b in enumerate(self.blocks):
-            self.gathered[bi].quantize_and_gather(self.opt.rank, b.param, self.w_g[bi, 0:1], self.w_g[bi, 1:2],
-                                                  self.pg)
+            gw = self.gathered[bi]
+            gw.quantize(self.opt.rank, b.param, self.w_g[bi, 0:1], self.w_g[bi, 1:2])
+            gw.gather_forward(self.opt.rank, b.param, self.pg)
+        for bi in reversed(range(self.n_blocks)):
+            self.gathered[bi].gather_transposed(self.opt.rank, self.pg)
 
     def gather_masters(self) -> List[tuple]:
         """Standard-layout fp32 (gamma, W_gu, W_down) of every block: the master
@@ -698,9 +736,7 @@ class NVFP4MLPStackTrainer:
         if self.opt is not None:
             self.opt.wait_all()
         for gw in self.gathered or ():
-            for w in gw.works:
-                w.wait()
-            gw.works = []
+            gw.wait()
 
     def flops_per_step(self, tokens: int) -> float:
         return 3 * 3 * 2.0 * tokens * self.d * self.f * self.n_blocks

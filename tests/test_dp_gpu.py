@@ -84,6 +84,7 @@ def _worker(rank, world, port, mode, out_path):
         for i, b in enumerate(tr.blocks):   # the NVFP4 weights the next step would use
             if tr.layout is not None:
                 q = tr.gathered[i].qweights(tr.w_g[i, 0:1], tr.w_g[i, 1:2])
+                tr.gathered[i].ensure_transposed()
             else:
                 q = mlp.quantize_weights(b.w_gu, b.w_down, g_gu=tr.w_g[i, 0:1], g_down=tr.w_g[i, 1:2])
             qws.append({k: getattr(q, k).cpu() for k in QFIELDS})

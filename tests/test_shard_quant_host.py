@@ -77,6 +77,7 @@ def test_gathered_pieces_assemble_the_full_weights(mlp, d, f, world):
             ps[r] = torch.from_numpy(s.reshape(ps.shape[1:]))
     gw.permuted = False
     qw = gw.qweights(torch.tensor([g_gu]), torch.tensor([g_dn]))
+    gw.ensure_transposed()
     for q, s, x, g in ((qw.q_gu, qw.s_gu, bits(w_gu), g_gu), (qw.q_down, qw.s_down, bits(w_down), g_dn),
                        (qw.q_gu_t, qw.s_gu_t, np.ascontiguousarray(bits(w_gu).T), g_gu),
                        (qw.q_down_t, qw.s_down_t, np.ascontiguousarray(bits(w_down).T), g_dn)):
