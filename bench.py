@@ -528,6 +528,10 @@ def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=No
         bd = step_breakdown(trainer, x, dy, n_blocks, d, f, min(micro_tokens, t_local), wgrad_splits=splits)
         if world > 1:
             bd["exposed_comm_ms_max_over_ranks"] = max_over_ranks(bd.get("exposed_comm_ms", 0.0), world)
+            # rank imbalance: a rank whose kernels finish early waits inside the next collective
+            cb = bd.get("compute_busy_ms", 0.0)
+            bd["compute_busy_ms_max_over_ranks"] = max_over_ranks(cb, world)
+            bd["compute_busy_ms_min_over_ranks"] = -max_over_ranks(-cb, world)
         res["kernel_breakdown"] = bd
     del trainer
     torch.cuda.empty_cache()
