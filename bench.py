@@ -490,6 +490,10 @@ def bench_mlp(pkg, args, world, rank, n_blocks, d, f, global_tokens, seed, pg=No
            "flops_per_step": flops, "n_gpus": world, "tokens_global": global_tokens, "tokens_per_rank": t_local,
            "micro_tokens": micro_tokens, "clocks": clk.summary(), "finite": bool(torch.isfinite(r).all().item())}
     if world > 1:
+        # under the power cap each GPU settles at its own clock; the step runs at the slowest
+        own = res["clocks"].get("sm_mhz") or 0.0
+        res["clocks"]["sm_mhz_min_over_ranks"] = -max_over_ranks(-float(own), world)
+        res["clocks"]["sm_mhz_max_over_ranks"] = max_over_ranks(float(own), world)
         if trainer.layout is not None:
             res["exchange"] = ("ZeRO-1: reduce-scatter + sharded AdamW, each rank quantizes its rows of the "
                                "updated weights, all-gather of NVFP4 weights")
