@@ -350,12 +350,6 @@ class GatheredWeights:
         self.works_t = [dist.all_gather_into_tensor(buf.view(-1), buf[rank].view(-1), group=pg, async_op=True)
                         for buf in (self.pq_gu_t, self.ps_gu_t, self.pq_down_t, self.ps_down_t)]
 
-    def quantize_and_gather(self, rank: int, param: torch.Tensor, g_gu: torch.Tensor, g_down: torch.Tensor,
-                            pg) -> None:
-        self.quantize(rank, param, g_gu, g_down)
-        self.gather_forward(rank, param, pg)
-        self.gather_transposed(rank, pg)
-
     def wait(self) -> None:
         """Make the current stream wait for every gather of the block still in flight."""
         for w in self.works + self.works_t:

@@ -4,7 +4,9 @@ Two ranks each take half of a 512-token batch; the single-rank trainer runs
 the same batch as two micro-batches of the same 256 tokens, so every global
 scale of every GEMM operand is the same in both runs.  Three exchanges run:
 ZeRO-1 with sharded weight quantization (rank-major buckets, NVFP4 weights
-gathered), ZeRO-1 gathering bf16 parameters, and all-reduce.  Checks:
+gathered), ZeRO-1 gathering bf16 parameters, and all-reduce, each with one
+micro-batch per rank (wgrads written into the bf16 bucket) and two (fp32
+accumulators copied into it).  Checks:
 
 * all three give bit-identical fp32 master weights after two steps (a sum of
   two bf16 gradients does not depend on the collective; the AdamW update is
@@ -31,6 +33,7 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 T_LOCAL, D, F, BLOCKS = 256, 256, 512, 2
 MODES = ("zero_sq", "zero_flat", "allreduce")
+RUNS = [(m, T_LOCAL) for m in MODES] + [("zero_sq", T_LOCAL // 2), ("allreduce", T_LOCAL // 2)]   # (mode, micro)
 QFIELDS = ("g_gu", "g_down", "q_gu", "s_gu", "q_down", "s_down", "q_gu_t", "s_gu_t", "q_down_t", "s_down_t")
 
 
@@ -57,7 +60,7 @@ def _mlp():
     return importlib.import_module("nvfp4_b200.mlp")
 
 
-def _worker(rank, world, port, mode, out_path):
+def _worker(rank, world, port, mode, micro, out_path):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -70,7 +73,7 @@ def _worker(rank, world, port, mode, out_path):
         x, dy = _batch(world)
         lo, hi = rank * T_LOCAL, (rank + 1) * T_LOCAL
         sq = {"zero_sq": True, "zero_flat": False, "allreduce": None}[mode]
-        tr = mlp.NVFP4MLPStackTrainer(BLOCKS, D, F, seed=7, micro_tokens=T_LOCAL, max_local_tokens=T_LOCAL,
+        tr = mlp.NVFP4MLPStackTrainer(BLOCKS, D, F, seed=7, micro_tokens=micro, max_local_tokens=T_LOCAL,
                                       process_group=dist.group.WORLD, zero=mode != "allreduce", shard_quant=sq)
         assert (tr.layout is not None) == (mode == "zero_sq")
         p0 = [tuple(t.cpu() for t in m) for m in tr.gather_masters()]
@@ -107,19 +110,22 @@ def test_two_rank_trainer_matches_single_rank(pkg, tmp_path):
     import torch.multiprocessing as mp
     world = 2
     res = {}
-    for mode in MODES:
-        path = str(tmp_path / f"{mode}.pt")
-        mp.spawn(_worker, args=(world, _free_port(), mode, path), nprocs=world, join=True)
-        res[mode] = torch.load(path)
-        assert res[mode]["device_error"] == 0
-    ref = res["allreduce"]
-    for mode in ("zero_sq", "zero_flat"):
-        for a, b in zip(res[mode]["masters"], ref["masters"]):
+    for mode, micro in RUNS:
+        path = str(tmp_path / f"{mode}_{micro}.pt")
+        mp.spawn(_worker, args=(world, _free_port(), mode, micro, path), nprocs=world, join=True)
+        res[mode, micro] = torch.load(path)
+        assert res[mode, micro]["device_error"] == 0
+    for (mode, micro) in RUNS:
+        if mode == "allreduce":
+            continue
+        ref = res["allreduce", micro]
+        for a, b in zip(res[mode, micro]["masters"], ref["masters"]):
             for x, y in zip(a, b):
-                assert torch.equal(x.view(torch.int32), y.view(torch.int32)), mode
-        for qa, qb in zip(res[mode]["qws"], ref["qws"]):
+                assert torch.equal(x.view(torch.int32), y.view(torch.int32)), (mode, micro)
+        for qa, qb in zip(res[mode, micro]["qws"], ref["qws"]):
             for k in QFIELDS:
-                assert torch.equal(qa[k], qb[k]), (mode, k)
+                assert torch.equal(qa[k], qb[k]), (mode, micro, k)
+    ref = res["allreduce", T_LOCAL]
 
     mlp = _mlp()
     x, dy = _batch(world)
