@@ -83,3 +83,21 @@ def test_gathered_pieces_assemble_the_full_weights(mlp, d, f, world):
                        (qw.q_down_t, qw.s_down_t, np.ascontiguousarray(bits(w_down).T), g_dn)):
         oq, os_ = orc.quant_nvfp4(x, g)
         assert np.array_equal(q.numpy(), oq) and np.array_equal(s.numpy().reshape(-1), os_.reshape(-1))
+
+
+def test_quantizer_out_buffers_checked(pkg):
+    """ops.quantize / quantize_t accept caller buffers (slots of a gather
+    buffer) only with the exact shape, dtype, device and contiguity."""
+    import importlib
+    ops = importlib.import_module("nvfp4_b200.ops")
+    q_shape, s_shape = (256, 64), ops.scale_shape(256, 128)
+    q = torch.empty(q_shape, dtype=torch.uint8)
+    s = torch.empty(s_shape, dtype=torch.uint8)
+    assert ops._outputs((q, s), q_shape, s_shape, q.device)[0] is q
+    big = torch.empty((512, 64), dtype=torch.uint8)
+    assert ops._outputs((big[128:384], s), q_shape, s_shape, q.device)[0].data_ptr() == big[128].data_ptr()
+    for bad in ((q.float(), s), (q[:, :32], s), (q, s[:128]), (big[:, ::2][:256, :32], s)):
+        with pytest.raises(RuntimeError):
+            ops._outputs(bad, q_shape, s_shape, q.device)
+    q2, s2 = ops._outputs(None, q_shape, s_shape, q.device)
+    assert q2.shape == q_shape and s2.shape == s_shape and q2.dtype == torch.uint8
