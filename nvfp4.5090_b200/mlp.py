@@ -36,8 +36,8 @@ NVFP4MLPStackTrainer keeps W_gu interleaved.
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass, field
-from typing import Dict, List, Optional
+from dataclasses import dataclass
+from typing import List, Optional
 
 import torch
 import torch.nn as nn

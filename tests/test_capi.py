@@ -1,6 +1,5 @@
 """CPU tests of the C ABI: the library loads, exports every symbol the header
 declares, and rejects invalid arguments before touching any device."""
-import ctypes
 import os
 import re
 

@@ -2,7 +2,6 @@
 oracle's dequantize -> float64 matmul emulation.  Tolerance: relative
 Frobenius error <= 1e-2 on every bf16 output (intermediate bf16 rounding may
 flip single nibbles downstream; the stated bar absorbs that)."""
-import numpy as np
 import pytest
 import torch
 
