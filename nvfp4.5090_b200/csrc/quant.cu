@@ -529,9 +529,11 @@ __global__ void __launch_bounds__(256, BPT == 1 ? 4 : 1) rms_stats_kernel(const 
 // encode the current one: thread (qtr, p) owns output rows d0 + 2p, 2p + 1
 // (input columns) and the blocks 2 qtr, 2 qtr + 1 of the tile (input rows
 // t0 + 32 qtr .. + 32), reads its column pair down the tile (a warp reads 128
-// contiguous bytes of a tile row) and writes 16 bytes of nibbles per output
-// row.  The tile's 2 scale atoms (1 KB) are staged in shared memory and
-// written whole.  Waits are bounded; a timeout sets g_quant_error.
+// contiguous bytes of a tile row) and produces 16 bytes of nibbles per output
+// row.  The nibbles (staged in the tile's input buffer once it is read) and
+// the tile's 2 scale atoms (1 KB) go out whole from shared memory, the
+// buffer's next load after that.  Waits are bounded; a timeout sets
+// g_quant_error.
 
 constexpr int TQ_T = 128;                  // input rows per tile = output k extent (8 blocks)
 constexpr int TQ_D = 128;                  // input columns per tile = output rows
@@ -660,25 +662,22 @@ __global__ void __launch_bounds__(256, 3) quant_t_kernel(
       codes_b |= cb << (8 * bi);
     }
     __syncthreads();  // every thread is done reading this buffer
-    if (tid == 0 && tile + 2 * (int)gridDim.x < n_tiles) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(tile + 2 * gridDim.x, buf);
-    }
-    // nibbles: output rows d0 + dl0 (+1), 16 bytes at byte column (t0 + 32 qtr) / 2
-    const int64_t tcol = t0 + 32 * qtr;
-    if (tcol < rows) {
-      const int64_t nbytes = imin64(16, (rows - tcol) >> 1);   // 16 or 8 (rows % 16 == 0)
+    // The tile's nibbles (128 output rows x 64 bytes: 16 per thread and row, at
+    // byte column 16 qtr) are staged in the input buffer just read, 16-byte
+    // column c of row r at c ^ ((r >> 1) & 3) (at most 2-way bank conflicts on
+    // the way in, none on the way out), and leave below as whole 32-byte
+    // sectors, two threads per output row: +3% (row scale + gamma) and +6%
+    // (plain) at 32768 x 4096 over each thread writing its 16-byte pieces of
+    // 128 output rows directly.  The buffer's next load goes out once the
+    // staged bytes are read.
+    {
+      uint8_t* nib = reinterpret_cast<uint8_t*>(sm.tile[buf]);
       const uint32_t* qw[2] = {qwa, qwb};
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        if (d0 + dl0 + h >= cols) continue;
-        uint8_t* dst = q + (d0 + dl0 + h) * (rows >> 1) + (tcol >> 1);
-        if (nbytes == 16 && q16) {
-          *reinterpret_cast<uint4*>(dst) = make_uint4(qw[h][0], qw[h][1], qw[h][2], qw[h][3]);
-        } else {
-          reinterpret_cast<uint2*>(dst)[0] = make_uint2(qw[h][0], qw[h][1]);
-          if (nbytes == 16) reinterpret_cast<uint2*>(dst)[1] = make_uint2(qw[h][2], qw[h][3]);
-        }
+        const int r = dl0 + h;
+        const int c = qtr ^ ((r >> 1) & 3);
+        *reinterpret_cast<uint4*>(nib + r * 64 + c * 16) = make_uint4(qw[h][0], qw[h][1], qw[h][2], qw[h][3]);
       }
     }
     // scale codes: output row dl, blocks 2 qtr, 2 qtr + 1 = atom qtr / 2, columns (2 qtr) % 4 + 0, 1
@@ -692,6 +691,35 @@ __global__ void __launch_bounds__(256, 3) quant_t_kernel(
     const int64_t dst = ((int64_t)(tile / n_tiles_t) * (pad_cols_out >> 2) + atom0) * 512;
     if ((int64_t)tid * 4 < n_atoms * 512)
       *reinterpret_cast<uint32_t*>(s + dst + tid * 4) = reinterpret_cast<const uint32_t*>(sm.atoms[buf])[tid];
+    {
+      // thread tid writes output row d0 + tid / 2, bytes [32 (tid & 1), +32) of the tile's 64
+      const int r = tid >> 1, hb = tid & 1;
+      const uint8_t* nib = reinterpret_cast<const uint8_t*>(sm.tile[buf]);
+      const int64_t orow = d0 + r;
+      const int64_t bcol = (t0 >> 1) + 32 * hb;            // byte column in the output row
+      const int64_t avail = (rows >> 1) - bcol;             // bytes of this half inside the row (a multiple of 8)
+      if (orow < cols && avail > 0) {
+        uint8_t* dstp = q + orow * (rows >> 1) + bcol;
+        const int ca = (2 * hb) ^ ((r >> 1) & 3), cb = (2 * hb + 1) ^ ((r >> 1) & 3);
+        const uint4 va = *reinterpret_cast<const uint4*>(nib + r * 64 + ca * 16);
+        const uint4 vb = *reinterpret_cast<const uint4*>(nib + r * 64 + cb * 16);
+        if (avail >= 32 && q16) {
+          reinterpret_cast<uint4*>(dstp)[0] = va;
+          reinterpret_cast<uint4*>(dstp)[1] = vb;
+        } else {   // 8-byte granules: output rows only 8-byte aligned, or the row ends inside this half
+          const uint2 w[4] = {make_uint2(va.x, va.y), make_uint2(va.z, va.w), make_uint2(vb.x, vb.y),
+                              make_uint2(vb.z, vb.w)};
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (avail >= 8 * (i + 1)) reinterpret_cast<uint2*>(dstp)[i] = w[i];
+        }
+      }
+    }
+    __syncthreads();   // the staged nibbles are read before the buffer is loaded again
+    if (tid == 0 && tile + 2 * (int)gridDim.x < n_tiles) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(tile + 2 * gridDim.x, buf);
+    }
   }
   if (!ok && tid == 0) {
     atomicExch(&g_quant_error, NVFP4B200_ERR_TIMEOUT);
