@@ -95,13 +95,15 @@ constexpr int QT_COLS = 512;       // 32 blocks = 8 scale atoms
 constexpr int QT_THREADS = 256;    // 8 warps x 16 rows
 
 
-// The scaled variants (row scale and / or gamma) keep 2 rows per pass and are
-// capped at 80 registers for 3 CTAs per SM: +34% over 4 rows per pass at 131
+// The scaled variants (row scale and / or gamma) keep 2 rows per pass: at
+// 80 registers and 3 CTAs per SM that was +34% over 4 rows per pass at 131
 // registers (2 CTAs per SM), where each CTA's cold first load was exposed.
-// The plain variant is capped at 64 registers for 4 CTAs per SM (no spills):
-// +3% at 32768 x 4096 and 16384 x 8192 over 68 registers and 3 CTAs.
+// Both kinds are capped at 64 registers for 4 CTAs per SM: the plain variant
+// without spills (+3% at 32768 x 4096 and 16384 x 8192 over 68 registers and
+// 3 CTAs), the scaled ones with 84 bytes of spills (+3% over 80 registers and
+// 3 CTAs at those shapes; small inputs of a few hundred rows lose ~5%).
 template <bool HAS_ROW, bool HAS_GAMMA>
-__global__ void __launch_bounds__(QT_THREADS, (HAS_ROW || HAS_GAMMA) ? 3 : 4) quant_tile_kernel(
+__global__ void __launch_bounds__(QT_THREADS, 4) quant_tile_kernel(
     const uint16_t* __restrict__ x, const float* __restrict__ row_scale,
     const uint16_t* __restrict__ gamma, uint8_t* __restrict__ q, uint8_t* __restrict__ s,
     int64_t rows, int64_t k, int64_t pad_cols, const float* __restrict__ gptr, int q8) {
