@@ -163,6 +163,16 @@ __global__ void __launch_bounds__(RB_THREADS) rmsnorm_bwd_kernel(
   int buf = 0;
   for (int64_t r = r_begin; r < r_end; ++r) {
     load(r + 1, nx, nd);
+    // the residual gradient is read at the top of the row, so its latency
+    // hides behind the reduction (read after the barrier it was exposed once
+    // per row: 262 vs 213 us at 16384 x 8192, 123 vs 115 us at 16384 x 4096)
+    uint4 cr[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int64_t col = (int64_t)v * 4096 + 8 * tid;
+      cr[v] = make_uint4(0, 0, 0, 0);
+      if (dres && col < k) cr[v] = __ldg(reinterpret_cast<const uint4*>(dres + r * k + col));
+    }
     const float inv = __ldg(inv_rms + r);
     float part = 0.0f;
 #pragma unroll
@@ -198,7 +208,7 @@ __global__ void __launch_bounds__(RB_THREADS) rmsnorm_bwd_kernel(
         o[j] = inv * (d * gam[v][j] - xn * mean);
       }
       if (dres) {
-        const uint4 rv = __ldg(reinterpret_cast<const uint4*>(dres + r * k + col));
+        const uint4 rv = cr[v];
         const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
