@@ -84,9 +84,8 @@ __global__ void __launch_bounds__(256) global_amax_kernel(const uint4* __restric
 // tile quantizer: 128 rows x 512 columns per CTA
 // ---------------------------------------------------------------------------
 // Each lane owns one 16-element block column of the tile (32 B of every row);
-// a warp covers 16 rows, read a few rows per pass (2 for the plain quantizer,
-// 4 with row scale or gamma: measured best for each) with the next pass's
-// loads in flight while the current one is encoded.  Per row a warp reads 1 KB and
+// a warp covers 16 rows, read 2 rows per pass with the next pass's loads in
+// flight while the current one is encoded.  Per row a warp reads 1 KB and
 // writes 256 B of nibbles; the tile's 8 scale atoms (4 KB, contiguous in the
 // swizzled layout) are staged in shared memory and written whole.
 
