@@ -6,10 +6,11 @@
 // semantics, E4M3 block scale by cvt.rn.satfinite, reciprocal-then-multiply,
 // the away-from-zero E2M1 ladder, low-nibble-first packing and the 128x4
 // swizzled scale layout -- see common.cuh for each helper.  What differs is
-// the data movement: warps read 512 contiguous bytes per instruction, write
-// 128 contiguous bytes of nibbles, and scale atoms are staged in shared
-// memory and written as whole 512-byte atoms, so no separate zero-fill of
-// the scale tensor is needed.
+// the data movement: warps read 512 contiguous bytes per instruction and
+// write 256 contiguous bytes of nibbles (the transposed quantizer stages a
+// tile's nibbles in shared memory and writes whole 32-byte sectors), and
+// scale atoms are staged in shared memory and written as whole 512-byte
+// atoms, so no separate zero-fill of the scale tensor is needed.
 #include "common.cuh"
 
 #include <cuda.h>
