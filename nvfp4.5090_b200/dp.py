@@ -1,11 +1,10 @@
 """Data-parallel plumbing of the NVFP4 MLP training step.
 
-The token dimension is sharded across ranks (one process per GPU); every
-rank holds the bf16 weights and re-quantizes them, so the only exchanges are
-on the weight gradients.  Two schemes, both over NCCL (NVLink / NVSwitch)
-through torch.distributed with one bucket per MLP block, launched as soon as
-that block's wgrad GEMMs are enqueued so the transfer overlaps the backward
-of the blocks below:
+The token dimension is sharded across ranks (one process per GPU).  The
+weight gradients are exchanged over NCCL (NVLink / NVSwitch) through
+torch.distributed with one bucket per MLP block, launched as soon as that
+block's wgrad GEMMs are enqueued so the transfer overlaps the backward of
+the blocks below.  Two schemes:
 
 * ``BucketAllReducer``: SUM all-reduce of each gradient bucket; every rank
   then runs the full optimizer update.
@@ -14,6 +13,9 @@ of the blocks below:
   only for the shard), then an all-gather of the updated parameter shards.
   The per-step optimizer work and memory then fall as 1/world; the gathers
   are waited for lazily, right before a block's weights are next used.
+  (``mlp.GatheredWeights`` goes one step further for the MLP trainer: each
+  rank quantizes its shard's rows and the ranks all-gather NVFP4 weights
+  instead of bf16 parameters.)
 
 The reference has no distributed code; this module is new.
 """
