@@ -1,8 +1,9 @@
 """Data-parallel host logic on CPU with gloo process groups of 2 and 4 ranks:
 bucketed async all-reduce, mean-gradient scaling, the ZeRO-1 sharded
 optimizer (reduce-scatter, shard update, all-gather) against the all-reduce
-path, and host-side failure detection (a rank that dies before the
-collective)."""
+path, the gathers of sharded NVFP4 weights (GatheredWeights with the oracle
+standing in for the GPU quantizer), and host-side failure detection (a rank
+that dies before the collective)."""
 import datetime
 import os
 import socket
@@ -128,6 +129,77 @@ def _worker_sharded(rank, world, port, q):
         q.put((rank, traceback.format_exc()))
 
 
+def _worker_gathered(rank, world, port, q):
+    """Each rank quantizes its rows of a block's weights (rank-major bucket)
+    through GatheredWeights.quantize, with the oracle in place of the GPU
+    quantizer, and the real gathers assemble the full NVFP4 weights; every
+    rank must then hold exactly the oracle's quantization of the whole
+    matrices, in both orientations, and the whole gamma.  Two rounds with
+    different weights check that the buffers and the permutation are redone."""
+    try:
+        _init(rank, world, port, 60)
+        sys.path.insert(0, ROOT)
+        import importlib
+
+        import numpy as np
+
+        import __graft_entry__
+        from oracle import nvfp4_oracle as orc
+        __graft_entry__.import_package()
+        mlp = importlib.import_module("nvfp4_b200.mlp")
+
+        def bits(t):
+            return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+        def fake(transposed):
+            def quantize(x, global_scale=None, out=None, **kw):
+                assert not kw and out is not None
+                xb = bits(x)
+                qn, sn = orc.quant_nvfp4(np.ascontiguousarray(xb.T) if transposed else xb,
+                                         np.float32(global_scale.item()))
+                out[0].copy_(torch.from_numpy(qn))
+                out[1].copy_(torch.from_numpy(sn).reshape(out[1].shape))
+                return out
+            return quantize
+
+        mlp.ops.quantize, mlp.ops.quantize_t = fake(False), fake(True)
+        d, f = {2: (256, 256), 3: (384, 192), 4: (512, 256)}[world]
+        lay = mlp.ShardQuantLayout(d, f, world)
+        gw = mlp.GatheredWeights(lay, "cpu")
+        for rnd in range(2):
+            gen = torch.Generator().manual_seed(11 + rnd)      # the same weights on every rank
+            gamma = (1 + 0.1 * torch.randn(d, generator=gen)).to(torch.bfloat16)
+            w_gu = ((0.05 + rnd) * torch.randn(2 * f, d, generator=gen)).to(torch.bfloat16)
+            w_down = ((0.05 + rnd) * torch.randn(d, f, generator=gen)).to(torch.bfloat16)
+            full = torch.zeros(lay.shard * world, dtype=torch.bfloat16)
+            lay.store(full, gamma, w_gu, w_down)
+            param = torch.zeros_like(full)                     # only this rank's shard is present
+            sl = slice(rank * lay.shard, (rank + 1) * lay.shard)
+            param[sl] = full[sl]
+            g_gu = orc.global_scale_of(orc.bf16_bits_to_f32(bits(w_gu)))
+            g_dn = orc.global_scale_of(orc.bf16_bits_to_f32(bits(w_down)))
+            tg_gu, tg_dn = torch.tensor([float(g_gu)]), torch.tensor([float(g_dn)])
+            gw.quantize(rank, param, tg_gu, tg_dn)
+            gw.gather_forward(rank, param, dist.group.WORLD)
+            gw.gather_transposed(rank, dist.group.WORLD)
+            qw = gw.qweights(tg_gu, tg_dn)
+            assert torch.equal(gw.gamma, gamma), ("gamma", rnd)
+            gw.ensure_transposed()
+            for name, qq, ss, x, g in (("gu", qw.q_gu, qw.s_gu, bits(w_gu), g_gu),
+                                       ("down", qw.q_down, qw.s_down, bits(w_down), g_dn),
+                                       ("gu_t", qw.q_gu_t, qw.s_gu_t, np.ascontiguousarray(bits(w_gu).T), g_gu),
+                                       ("down_t", qw.q_down_t, qw.s_down_t, np.ascontiguousarray(bits(w_down).T), g_dn)):
+                oq, os_ = orc.quant_nvfp4(x, g)
+                assert np.array_equal(qq.numpy(), oq), (name, rnd)
+                assert np.array_equal(ss.numpy().reshape(-1), os_.reshape(-1)), (name, rnd)
+            gw.wait()                                           # nothing left in flight
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
 def _worker_failure(rank, world, port, q):
     try:
         _init(rank, world, port, 4)
@@ -176,6 +248,12 @@ def test_bucketed_allreduce(world):
 @pytest.mark.parametrize("world", [2, 4])
 def test_sharded_optimizer_matches_allreduce(world):
     out = _run(_worker_sharded, world=world)
+    assert out == {r: "ok" for r in range(world)}, out
+
+
+@pytest.mark.parametrize("world", [2, 3, 4])
+def test_sharded_nvfp4_weight_gathers(world):
+    out = _run(_worker_gathered, world=world, timeout=120)
     assert out == {r: "ok" for r in range(world)}, out
 
 
