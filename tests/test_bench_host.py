@@ -1,7 +1,14 @@
 """CPU tests of bench.py's host logic: the clock record that decides whether a
-run is kept (median SM clock and the throttle reasons seen), and the reference
-arm's rank handling under torchrun (ranks other than 0 exit without work)."""
+run is kept (median SM clock and the throttle reasons seen), the reference
+arm's rank handling under torchrun (ranks other than 0 exit without work),
+the CPU baseline samples (the reference arm's GEMM tile is the oracle's NVFP4
+product of its operands), and the per-kernel step summaries."""
+import numpy as np
+import pytest
+import torch
+
 import bench
+from oracle import nvfp4_oracle as orc
 
 
 def _sampler(lines):
@@ -86,3 +93,42 @@ def test_kernel_summary_wgrad_splits():
     assert out["wgrad_gate_up"]["launches"] == 2 and abs(out["wgrad_gate_up"]["mean_ms"] - 0.4) < 1e-9
     assert out["bwd_dxn"]["launches"] == 2 and abs(out["bwd_dxn"]["mean_ms"] - 0.4) < 1e-9
     assert out["fwd_down"]["launches"] == 2 and abs(out["fwd_down"]["mean_ms"] - 0.2) < 1e-9
+
+
+@pytest.fixture
+def keep_torch_threads():
+    n = torch.get_num_threads()
+    yield
+    torch.set_num_threads(n)
+
+
+def test_cpu_gemm_sample_computes_its_tile(keep_torch_threads):
+    """The reference arm's tile (quantize both operands with their global
+    scales, dequantize, fp32 matmul, bf16) at a small size, against the
+    oracle's float64 emulation of the same NVFP4 GEMM: every element within
+    the GEMM parity bound 2^-8 |ref| + 2^-20 sum |terms|."""
+    rows, cols, k = 128, 64, 512
+    tflops, cores, secs, d = bench.cpu_gemm_sample(rows, cols, k, threads=2)
+    assert tflops > 0 and cores == 2 and secs > 0
+    assert d.shape == (rows, cols) and d.dtype == torch.bfloat16
+    g = torch.Generator().manual_seed(1)                  # the sample's own operands
+    a = torch.randn(rows, k, generator=g).to(torch.bfloat16)
+    b = torch.randn(cols, k, generator=g).to(torch.bfloat16)
+    bits = lambda t: t.view(torch.int16).numpy().view(np.uint16)
+    ga = orc.global_scale_of(a.float().numpy())
+    gb = orc.global_scale_of(b.float().numpy())
+    qa, sa = orc.quant_nvfp4(bits(a), ga)
+    qb, sb = orc.quant_nvfp4(bits(b), gb)
+    ref = orc.gemm_emulation_f64(qa, sa, qb, sb, rows, cols, k, output_scale=np.float32(ga) * np.float32(gb))
+    terms = (np.abs(orc.dequant_nvfp4(qa, sa, rows, k, ga)).astype(np.float64)
+             @ np.abs(orc.dequant_nvfp4(qb, sb, cols, k, gb)).astype(np.float64).T)
+    err = np.abs(d.float().numpy().astype(np.float64) - ref)
+    assert np.all(err <= 2.0 ** -8 * np.abs(ref) + 2.0 ** -20 * terms)
+    assert orc.rel_frobenius(d.float().numpy(), ref) < 1e-2
+
+
+def test_cpu_quant_and_mlp_samples_run_small(keep_torch_threads):
+    gbs, cores, secs = bench.cpu_quant_sample(rows=512, k=256, threads=2)
+    assert gbs > 0 and cores == 2 and secs > 0
+    tok_s, cores, secs = bench.cpu_mlp_sample(tokens=16, d=128, f=256, threads=2)
+    assert tok_s > 0 and cores == 2 and secs > 0
